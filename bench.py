@@ -1,0 +1,486 @@
+#!/usr/bin/env python
+"""Benchmark of the b200attn hot path (driver contract: one JSON line on rank 0).
+
+Default workload: BASELINE config 2, the reference's headline shape -- non-causal
+prefill forward, B=1, H=8, N=4096, D=64, fp16, returning O and L
+(bench/bench_fa3_headline.py of the reference times the same call, forward()+L).
+A step is one forward over one batch.  Other configs: --config 1|2|3|4|5a.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+
+Multi-GPU (torchrun, one rank per GPU): configs 1/2 run independent replicas
+(weak scaling); config 3 shards its 128 (b, h) units and configs 4/5a shard
+batch rows across ranks with no collective (strong scaling).  Time is device
+time over the K timed steps (CUDA events on the launching stream), max over
+ranks.  Inputs: seeded synthetic data of the configs' shapes; steps rotate over
+enough input sets that the bytes touched between reuses exceed the 126 MB L2.
+
+`--impl reference` times the reference's CPU path for the same metric: its
+naive attention (ref/naive_attn.py:10-38, restated in oracle/attention.py) in
+fp32 numpy on the host cores, one bounded sample of the workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "flashattn-cuda_b200"))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 2 ** 20
+METRIC = "prefill fwd TFLOP/s & % B200 BF16 peak; decode KV GB/s & % HBM; 1/2/4/8 GPU"
+
+
+# ------------------------------------------------------------------ workloads
+CONFIGS = {
+    "1": dict(kind="prefill", B=1, H=8, Hkv=8, N=1024, D=64, dtype="float16", causal=False,
+              shard=False, name="config1: prefill fwd B=1 H=8 N=1024 D=64 fp16 non-causal"),
+    "2": dict(kind="prefill", B=1, H=8, Hkv=8, N=4096, D=64, dtype="float16", causal=False,
+              shard=False, name="config2: prefill fwd B=1 H=8 N=4096 D=64 fp16 non-causal"),
+    "3": dict(kind="prefill", B=4, H=32, Hkv=32, N=8192, D=128, dtype="bfloat16", causal=True,
+              shard=True, name="config3: prefill fwd B=4 H=32 N=8192 D=128 bf16 causal"),
+    "4": dict(kind="decode", B=64, H=32, Hkv=8, L=16384, D=128, dtype="float16", splits=16,
+              shard=True, name="config4: split-KV GQA decode B=64 H=32 Hkv=8 L=16384 D=128 fp16"),
+    "5a": dict(kind="paged", B=128, H=32, Hkv=8, D=128, page=16, lmin=512, lmax=32768,
+               dtype="float16", pps=64, shard=True,
+               name="config5a: paged decode B=128 H=32 Hkv=8 D=128 fp16 page=16 len U[512,32768]"),
+}
+
+
+def prefill_flops(c, units):
+    """Algorithmic FLOPs: 4*N^2*D per (b,h) unit; causal counts 2*D*N*(N+1)."""
+    N, D = c["N"], c["D"]
+    per = 2 * D * N * (N + 1) if c["causal"] else 4 * N * N * D
+    return per * units
+
+
+def paged_lengths(c):
+    rng = np.random.default_rng(55)
+    return rng.integers(c["lmin"], c["lmax"] + 1, size=c["B"]).astype(np.int64)
+
+
+# ---------------------------------------------------------------- clock probe
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]),
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def read_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def read_traffic(key: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get(key)
+    return None
+
+
+# -------------------------------------------------------------- CPU baselines
+def cpu_sample(cfg_key: str, steps: int, warmup: int):
+    """Time the reference's CPU path (oracle port, fp32 numpy) on bounded samples.
+
+    Returns (value, unit, sample description, cores).
+    """
+    from oracle import attention as ora
+    c = CONFIGS[cfg_key]
+    cores = os.cpu_count() or 1
+    if c["kind"] == "prefill":
+        # one (b, h) head per step (rows limited for the causal N=8192 case)
+        N, D = c["N"], c["D"]
+        rows = min(N, 2048)
+        q = ora.seeded_normal((rows, D), 1)
+        k = ora.seeded_normal((N, D), 2)
+        v = ora.seeded_normal((N, D), 3)
+        off = N - rows
+        for i in range(warmup + steps):
+            if i == warmup:
+                start = time.perf_counter()
+            ora.attention_head(q, k, v, D ** -0.5, c["causal"], off, np.float32)
+        el = time.perf_counter() - start
+        # 4*D FLOPs per (query row, visible key); causal row g sees g+1 keys
+        keys = sum(off + r + 1 for r in range(rows)) if c["causal"] else rows * N
+        flops = 4 * D * keys * steps
+        return flops / el / 1e12, "TFLOP/s", \
+            f"one (b,h) head, {rows} query rows x {N} keys, fp32 numpy, per step", cores
+    # decode: one batch row per step
+    if c["kind"] == "decode":
+        L, D, Hkv, H = c["L"], c["D"], c["Hkv"], c["H"]
+    else:
+        L, D, Hkv, H = int(paged_lengths(c).mean()), c["D"], c["Hkv"], c["H"]
+    q = ora.seeded_normal((1, H, D), 1)
+    k = ora.seeded_normal((1, Hkv, L, D), 2)
+    v = ora.seeded_normal((1, Hkv, L, D), 3)
+    for i in range(warmup + steps):
+        if i == warmup:
+            start = time.perf_counter()
+        ora.decode(q, k, v, None, np.float32)
+    el = time.perf_counter() - start
+    byts = 2 * Hkv * L * D * 2 * steps  # fp16 K+V bytes of the sample
+    return byts / el / 1e9, "GB/s", f"one batch row (KV length {L}), fp32 numpy, per step", cores
+
+
+# ------------------------------------------------------------------ GPU arm
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import b200attn
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    c = CONFIGS[args.config]
+    tdt = torch.float16 if c["dtype"] == "float16" else torch.bfloat16
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    stream = torch.cuda.current_stream(dev)
+
+    # ---- build the per-rank workload and one step function (device-resident inputs)
+    if c["kind"] == "prefill":
+        units = c["B"] * c["H"]
+        B = c["B"]
+        if c["shard"]:
+            assert c["B"] * c["H"] % world == 0
+            units //= world
+            Bl, Hl = (1, units) if units < c["H"] else (units // c["H"], c["H"])
+        else:
+            Bl, Hl = c["B"], c["H"]
+        shape = (Bl, Hl, c["N"], c["D"])
+        set_bytes = 4 * np.prod(shape) * 2
+        nsets = max(1, int(np.ceil(1.5 * L2_BYTES / set_bytes))) if set_bytes < L2_BYTES else 1
+        sets = [[torch.randn(shape, device=dev, generator=gen).to(tdt) for _ in range(3)]
+                for _ in range(nsets)]
+        flops = prefill_flops(c, Bl * Hl)
+        work_per_step = flops
+        unit = "TFLOP/s"
+
+        def step(i):
+            q, k, v = sets[i % nsets]
+            return b200attn.forward(q, k, v, causal=c["causal"])
+
+        kernel_regex = "prefill_fwd_kernel"
+        bound, peak = "tensor", None
+        h2d = 3 * int(np.prod(shape)) * 2
+        d2h = int(np.prod(shape)) * 2 + int(np.prod(shape[:3])) * 4
+        host_in = [torch.randn(shape, generator=torch.Generator().manual_seed(rank)).to(tdt)
+                   .pin_memory() for _ in range(3)]
+        host_out = (torch.empty(shape, dtype=tdt).pin_memory(),
+                    torch.empty(shape[:3], dtype=torch.float32).pin_memory())
+
+        def e2e_step(i):
+            q = host_in[0].to(dev, non_blocking=True)
+            k = host_in[1].to(dev, non_blocking=True)
+            v = host_in[2].to(dev, non_blocking=True)
+            O, L = b200attn.forward(q, k, v, causal=c["causal"])
+            host_out[0].copy_(O, non_blocking=True)
+            host_out[1].copy_(L, non_blocking=True)
+
+        workload = dict(workload=c["name"], B=Bl, H=Hl, N=c["N"], D=c["D"],
+                        causal=c["causal"], dtype=c["dtype"], units_per_rank=Bl * Hl)
+    elif c["kind"] == "decode":
+        B = c["B"] // world if c["shard"] else c["B"]
+        H, Hkv, L, D = c["H"], c["Hkv"], c["L"], c["D"]
+        q = torch.randn(B, H, 1, D, device=dev, generator=gen).to(tdt)
+        k = torch.randn(B, Hkv, L, D, device=dev, generator=gen).to(tdt)
+        v = torch.randn(B, Hkv, L, D, device=dev, generator=gen).to(tdt)
+        work_per_step = 2 * B * Hkv * L * D * 2  # K+V bytes (fp16)
+        unit = "GB/s"
+        nsets = 1  # 4.3 GB of KV per step >> L2
+
+        def step(i):
+            return b200attn.decode(q, k, v, splits=c["splits"])
+
+        kernel_regex = "decode_kernel"
+        bound = "hbm"
+        h2d = B * H * D * 2
+        d2h = B * H * D * 2 + B * H * 4
+        host_q = torch.randn(B, H, 1, D).to(tdt).pin_memory()
+        host_out = (torch.empty(B, H, 1, D, dtype=tdt).pin_memory(),
+                    torch.empty(B, H, 1, dtype=torch.float32).pin_memory())
+
+        def e2e_step(i):
+            qd = host_q.to(dev, non_blocking=True)
+            O, Lo = b200attn.decode(qd, k, v, splits=c["splits"])
+            host_out[0].copy_(O, non_blocking=True)
+            host_out[1].copy_(Lo, non_blocking=True)
+
+        workload = dict(workload=c["name"], B=B, H=H, Hkv=Hkv, L=L, D=D, splits=c["splits"],
+                        dtype=c["dtype"], kv_cache="resident (4.3 GB/step > L2)")
+    else:  # paged
+        lens_all = paged_lengths(c)
+        # greedy balance of sequences over ranks by total length
+        order = np.argsort(-lens_all)
+        loads = [0] * world
+        mine = []
+        for idx in order:
+            r = int(np.argmin(loads))
+            loads[r] += lens_all[idx]
+            if r == rank:
+                mine.append(idx)
+        lens = lens_all[sorted(mine)]
+        B, H, Hkv, D, page = len(lens), c["H"], c["Hkv"], c["D"], c["page"]
+        npages = -(-lens // page)
+        P = int(npages.sum())
+        perm = torch.randperm(P, generator=torch.Generator().manual_seed(77 + rank)).to(torch.int32)
+        bt = torch.zeros(B, int(npages.max()), dtype=torch.int32)
+        pos = 0
+        for b in range(B):
+            bt[b, :npages[b]] = perm[pos:pos + npages[b]]
+            pos += npages[b]
+        bt = bt.to(dev)
+        kl = torch.tensor(lens, dtype=torch.int32, device=dev)
+        kp = torch.randn(P, Hkv, page, D, device=dev, generator=gen).to(tdt)
+        vp = torch.randn(P, Hkv, page, D, device=dev, generator=gen).to(tdt)
+        q = torch.randn(B, H, 1, D, device=dev, generator=gen).to(tdt)
+        work_per_step = int(lens.sum()) * Hkv * D * 2 * 2
+        unit = "GB/s"
+        nsets = 1
+
+        def step(i):
+            return b200attn.decode_paged(q, kp, vp, bt, kl, pages_per_split=c["pps"])
+
+        kernel_regex = "decode_kernel"
+        bound = "hbm"
+        h2d = B * H * D * 2
+        d2h = B * H * D * 2 + B * H * 4
+        host_q = torch.randn(B, H, 1, D).to(tdt).pin_memory()
+        host_out = (torch.empty(B, H, 1, D, dtype=tdt).pin_memory(),
+                    torch.empty(B, H, 1, dtype=torch.float32).pin_memory())
+
+        def e2e_step(i):
+            qd = host_q.to(dev, non_blocking=True)
+            O, Lo = b200attn.decode_paged(qd, kp, vp, bt, kl, pages_per_split=c["pps"])
+            host_out[0].copy_(O, non_blocking=True)
+            host_out[1].copy_(Lo, non_blocking=True)
+
+        workload = dict(workload=c["name"], B=B, total_tokens=int(lens.sum()),
+                        pages=P, pages_per_split=c["pps"], dtype=c["dtype"])
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    # ---- warm-up
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+
+    # ---- timed device-resident region
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize(dev)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    # per-launch events for the dominant kernel (same stream)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    ev0.record(stream)
+    for i in range(args.steps):
+        kev[i][0].record(stream)
+        step(args.warmup + i)
+        kev[i][1].record(stream)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    step_ms = [a.elapsed_time(b) for a, b in kev]
+
+    # ---- end-to-end through the public API with host buffers
+    for i in range(2):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+
+    # ---- max over ranks
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+
+    scale = 1e12 if unit == "TFLOP/s" else 1e9
+    total_work = work_per_step * args.steps * world
+    value = total_work / (ms / 1e3) / scale
+    e2e_value = total_work / (e2e_ms / 1e3) / scale
+
+    peaks = read_peaks()
+    kernel_ms = statistics.median(step_ms)
+    achieved = work_per_step / (kernel_ms / 1e3) / scale
+    if bound == "tensor":
+        pk = peaks["bf16_tflops"]
+        runit = "TFLOP/s"
+    else:
+        pk = peaks["hbm_gbs"]
+        runit = "GB/s"
+    roofline = {"bound": bound, "achieved": round(achieved, 2), "peak": pk, "unit": runit,
+                "frac": round(achieved / pk, 4), "traffic": read_traffic(f"config{args.config}"),
+                "peak_source": peaks["source"] + (" (burst)" if bound == "tensor" else ""),
+                "kernel": kernel_regex, "launch_ms_median": round(kernel_ms, 5),
+                "note": "achieved = algorithmic work per step / median per-step device time "
+                        "(CUDA events on the launching stream)"}
+
+    out = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            v, u, sample, cores = cpu_sample(args.config, steps=2, warmup=1)
+            cpu = {"value": round(v, 6), "unit": u, "cores": cores, "kind": "port",
+                   "sample": sample}
+        kernel_launches = args.steps * (1 if c["kind"] == "prefill" else 2)
+        out = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": unit,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 5),
+            "higher_is_better": True,
+            "scaling": "weak" if not c["shard"] else "strong",
+            "vs_baseline": None,
+            "dtype": "f16" if c["dtype"] == "float16" else "bf16",
+            "data": "synthetic (seeded N(0,1), generated on device)",
+            "config": {**workload,
+                       "l2": f"{nsets} rotating input sets" if nsets > 1 else
+                             "inputs larger than L2",
+                       "parallelism": ("replicas" if not c["shard"] else "sharded") +
+                                      f" x{world}"},
+            "e2e": {"value": round(e2e_value, 3), "unit": unit,
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "gpu_launches": kernel_launches,
+            "clocks": clocks,
+        }
+    return out
+
+
+def run_reference(args, rank, world):
+    """Reference arm: the reference's CPU naive attention (oracle port) on rank 0 only."""
+    if rank != 0:
+        return None
+    c = CONFIGS[args.config]
+    v, unit, sample, cores = cpu_sample(args.config, steps=args.steps, warmup=args.warmup)
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(v, 6),
+        "unit": unit,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak" if not c["shard"] else "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": c["name"], "sample": sample},
+        "cpu_baseline": {"value": round(v, 6), "unit": unit, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(v, 6), "unit": unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        out = run_reference(args, rank, world)
+    else:
+        if world > 1:
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+        out = run_ours(args, rank, world, local_rank)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,67 @@
+"""ctypes binding of libb200attn.so (the extern "C" ABI in include/b200attn.h).
+
+The library is loaded from this package directory only.  If it is missing the
+import fails loudly: there is no CPU or eager fallback for any entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libb200attn.so")
+
+B2A_OK = 0
+B2A_F16 = 0
+B2A_BF16 = 1
+
+_c_int, _c_float, _vp = ctypes.c_int, ctypes.c_float, ctypes.c_void_p
+
+_SIGNATURES = {
+    "b2a_status_string": (ctypes.c_char_p, [_c_int]),
+    "b2a_last_error": (ctypes.c_char_p, []),
+    "b2a_version": (ctypes.c_char_p, []),
+    # q k v o lse | B H Hkv N D | dtype causal scale stream
+    "b2a_prefill_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp] + [_c_int] * 5
+                        + [_c_int, _c_int, _c_float, _vp]),
+    # q k v o_part l_part | B H Hkv Lkv D splits | dtype scale stream
+    "b2a_decode_splitkv": (_c_int, [_vp] * 5 + [_c_int] * 6 + [_c_int, _c_float, _vp]),
+    # o_part l_part o lse | B H splits D dtype | stream
+    "b2a_decode_combine": (_c_int, [_vp] * 4 + [_c_int] * 5 + [_vp]),
+    # q kp vp bt lens o_part l_part o lse | B H Hkv D page max_pages num_pages pps | dtype scale stream
+    "b2a_decode_paged": (_c_int, [_vp] * 9 + [_c_int] * 8 + [_c_int, _c_float, _vp]),
+    "b2a_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint32)]),
+}
+
+EXPORTED = tuple(_SIGNATURES)
+
+_lib = None
+
+
+def lib_path() -> str:
+    return _LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load libb200attn.so (once) and declare every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(_LIB_PATH):
+        raise RuntimeError(
+            f"b200attn: {_LIB_PATH} is missing; build it with `python -m b200attn.build` "
+            "(there is no fallback implementation)")
+    lib = ctypes.CDLL(_LIB_PATH)
+    for name, (res, args) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(status: int) -> None:
+    """Raise RuntimeError with the library's message for a non-OK status."""
+    if status != B2A_OK:
+        lib = load()
+        msg = lib.b2a_last_error().decode() or lib.b2a_status_string(status).decode()
+        raise RuntimeError(msg)

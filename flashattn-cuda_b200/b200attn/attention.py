@@ -1,0 +1,236 @@
+"""Reference-facing attention API over libb200attn.so.
+
+`forward` and `forward_only` keep the surface of the reference's extension
+module (cuda/flash_attn_fa3_db_full.cu:405-418): `forward(Q, K, V)` returns the
+list `[O, L]` (O in the compute dtype, L fp32 natural-log logsumexp
+[B, H, N]) and `forward_only(Q, K, V)` returns O.  Checks and their messages
+follow the reference's host function (cuda/flash_attn_fa3_db_full.cu:352-363);
+like it, inputs of any other dtype are cast to fp16 and non-contiguous inputs
+are copied (:366-368), and the launch goes on the current stream of Q's device
+under a device guard (:365, :380).
+
+Additions over the reference, all opt-in: bf16 inputs compute and return bf16
+(the reference would cast them to fp16), D = 128, `causal=True`, an explicit
+`scale`, GQA (K/V with fewer heads than Q), and the decode entry points
+`decode_splitkv`, `decode_combine`, `decode` and `decode_paged`.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float16: _lib.B2A_F16, torch.bfloat16: _lib.B2A_BF16}
+
+
+def _compute_dtype(t: torch.Tensor) -> torch.dtype:
+    return t.dtype if t.dtype in _DT else torch.float16
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _prefill(Q, K, V, want_L: bool, causal: bool, scale: Optional[float]):
+    if not (Q.is_cuda and K.is_cuda and V.is_cuda):
+        raise RuntimeError("Q/K/V must be CUDA tensors")
+    if Q.dim() != 4:
+        raise RuntimeError("Q must be 4D [B, H, N, D]")
+    B, H, N, D = Q.shape
+    if D not in (64, 128):
+        raise RuntimeError("Head dimension must be 64 or 128")
+    if N <= 0:
+        raise RuntimeError("N must be > 0")
+    if (K.dim() != 4 or K.shape != V.shape or K.shape[0] != B or K.shape[2] != N
+            or K.shape[3] != D or K.shape[1] <= 0 or H % K.shape[1] != 0):
+        raise RuntimeError("K and V must have the same shape as Q (self-attention only)"
+                           " up to a KV head count that divides H")
+    if K.device != Q.device or V.device != Q.device:
+        raise RuntimeError("Q/K/V must be on the same device")
+    Hkv = K.shape[1]
+    dt = _compute_dtype(Q)
+    lib = _lib.load()
+    with torch.cuda.device(Q.device):
+        Qc = Q.to(dt).contiguous()
+        Kc = K.to(dt).contiguous()
+        Vc = V.to(dt).contiguous()
+        O = torch.empty((B, H, N, D), dtype=dt, device=Q.device)
+        L = torch.empty((B, H, N), dtype=torch.float32, device=Q.device) if want_L else None
+        s = float(D) ** -0.5 if scale is None else float(scale)
+        _lib.check(lib.b2a_prefill_fwd(
+            Qc.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), O.data_ptr(), _ptr(L),
+            B, H, Hkv, N, D, _DT[dt], int(bool(causal)), s, _stream(Q.device)))
+    return O, L
+
+
+def forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, causal: bool = False,
+            scale: Optional[float] = None) -> list:
+    """Attention forward returning [O, L] (reference `forward`)."""
+    O, L = _prefill(Q, K, V, True, causal, scale)
+    return [O, L]
+
+
+def forward_only(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, causal: bool = False,
+                 scale: Optional[float] = None) -> torch.Tensor:
+    """Attention forward returning O only (reference `forward_only`); bitwise equal to forward's O."""
+    O, _ = _prefill(Q, K, V, False, causal, scale)
+    return O
+
+
+# ---------------------------------------------------------------------------- decode
+
+def _decode_q(q: torch.Tensor):
+    """Accept q as [B, H, D] or [B, H, 1, D]; return ([B,H,D] view, had_len_dim)."""
+    if q.dim() == 4:
+        if q.shape[2] != 1:
+            raise RuntimeError("decode expects query length 1 ([B, H, 1, D])")
+        return q[:, :, 0, :], True
+    if q.dim() != 3:
+        raise RuntimeError("q must be [B, H, D] or [B, H, 1, D]")
+    return q, False
+
+
+def _check_decode_common(q, k, v):
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise RuntimeError("q/K/V must be CUDA tensors")
+    if k.device != q.device or v.device != q.device:
+        raise RuntimeError("q/K/V must be on the same device")
+    if k.shape != v.shape:
+        raise RuntimeError("K and V must have the same shape")
+
+
+def decode_splitkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, splits: int = 16,
+                   scale: Optional[float] = None):
+    """Split-KV decode partials.
+
+    q [B, H, D] (or [B, H, 1, D]); k, v [B, Hkv, Lkv, D] contiguous KV cache.
+    Returns (o_part fp32 [B, H, splits, D], l_part fp32 [B, H, splits]): per
+    split the softmax-normalised output and the natural-log sum of exp.
+    """
+    q3, _ = _decode_q(q)
+    _check_decode_common(q3, k, v)
+    if k.dim() != 4:
+        raise RuntimeError("K/V must be [B, Hkv, Lkv, D]")
+    B, H, D = q3.shape
+    Bk, Hkv, Lkv, Dk = k.shape
+    if Bk != B or Dk != D or Hkv <= 0 or H % Hkv != 0:
+        raise RuntimeError("K/V must be [B, Hkv, Lkv, D] with H a multiple of Hkv")
+    dt = _compute_dtype(q3)
+    lib = _lib.load()
+    with torch.cuda.device(q3.device):
+        qc = q3.to(dt).contiguous()
+        kc = k.to(dt).contiguous()
+        vc = v.to(dt).contiguous()
+        o_part = torch.empty((B, H, splits, D), dtype=torch.float32, device=q3.device)
+        l_part = torch.empty((B, H, splits), dtype=torch.float32, device=q3.device)
+        s = float(D) ** -0.5 if scale is None else float(scale)
+        _lib.check(lib.b2a_decode_splitkv(
+            qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o_part.data_ptr(), l_part.data_ptr(),
+            B, H, Hkv, Lkv, D, int(splits), _DT[dt], s, _stream(q3.device)))
+    return o_part, l_part
+
+
+def decode_combine(o_part: torch.Tensor, l_part: torch.Tensor,
+                   dtype: torch.dtype = torch.float16) -> list:
+    """LSE-weighted merge of split partials: returns [O (dtype) [B,H,D], L fp32 [B,H]]."""
+    if not (o_part.is_cuda and l_part.is_cuda):
+        raise RuntimeError("o_part/l_part must be CUDA tensors")
+    if o_part.dim() != 4 or l_part.shape != o_part.shape[:3]:
+        raise RuntimeError("o_part must be [B, H, S, D] and l_part [B, H, S]")
+    if dtype not in _DT:
+        raise RuntimeError("dtype must be torch.float16 or torch.bfloat16")
+    B, H, S, D = o_part.shape
+    lib = _lib.load()
+    with torch.cuda.device(o_part.device):
+        op = o_part.float().contiguous()
+        lp = l_part.float().contiguous()
+        O = torch.empty((B, H, D), dtype=dtype, device=o_part.device)
+        L = torch.empty((B, H), dtype=torch.float32, device=o_part.device)
+        _lib.check(lib.b2a_decode_combine(op.data_ptr(), lp.data_ptr(), O.data_ptr(),
+                                          L.data_ptr(), B, H, S, D, _DT[dtype],
+                                          _stream(o_part.device)))
+    return [O, L]
+
+
+def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, splits: int = 16,
+           scale: Optional[float] = None) -> list:
+    """Split-KV decode + combine: returns [O, L] shaped like q ([B,H,D] / [B,H,1,D])."""
+    q3, had_len = _decode_q(q)
+    o_part, l_part = decode_splitkv(q3, k, v, splits, scale)
+    O, L = decode_combine(o_part, l_part, _compute_dtype(q3))
+    if had_len:
+        return [O.unsqueeze(2), L.unsqueeze(2)]
+    return [O, L]
+
+
+def decode_paged(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                 block_table: torch.Tensor, kv_lens: torch.Tensor, pages_per_split: int = 64,
+                 scale: Optional[float] = None, scratch: Optional[Sequence[torch.Tensor]] = None
+                 ) -> list:
+    """Paged-KV decode: returns [O, L] shaped like q.
+
+    k_pool, v_pool: [P, Hkv, page_size, D]; block_table int32 [B, max_pages]
+    (page ids of each sequence in order); kv_lens int32 [B] (>= 1 each).
+    `scratch` may pass preallocated (o_part, l_part) buffers of shapes
+    [B, H, S, D] / [B, H, S] fp32 with S = ceil(max_pages / pages_per_split).
+    """
+    q3, had_len = _decode_q(q)
+    _check_decode_common(q3, k_pool, v_pool)
+    if k_pool.dim() != 4:
+        raise RuntimeError("k_pool/v_pool must be [P, Hkv, page_size, D]")
+    B, H, D = q3.shape
+    P, Hkv, page, Dk = k_pool.shape
+    if Dk != D or Hkv <= 0 or H % Hkv != 0:
+        raise RuntimeError("k_pool must be [P, Hkv, page_size, D] with H a multiple of Hkv")
+    if block_table.dim() != 2 or block_table.shape[0] != B or kv_lens.shape != (B,):
+        raise RuntimeError("block_table must be [B, max_pages] and kv_lens [B]")
+    if not (block_table.is_cuda and kv_lens.is_cuda):
+        raise RuntimeError("block_table/kv_lens must be CUDA tensors")
+    max_pages = block_table.shape[1]
+    S = (max_pages + pages_per_split - 1) // pages_per_split
+    dt = _compute_dtype(q3)
+    lib = _lib.load()
+    with torch.cuda.device(q3.device):
+        qc = q3.to(dt).contiguous()
+        kc = k_pool.to(dt).contiguous()
+        vc = v_pool.to(dt).contiguous()
+        bt = block_table.to(torch.int32).contiguous()
+        kl = kv_lens.to(torch.int32).contiguous()
+        if scratch is None:
+            o_part = torch.empty((B, H, S, D), dtype=torch.float32, device=q3.device)
+            l_part = torch.empty((B, H, S), dtype=torch.float32, device=q3.device)
+        else:
+            o_part, l_part = scratch
+            if o_part.shape != (B, H, S, D) or l_part.shape != (B, H, S):
+                raise RuntimeError("scratch buffers have the wrong shape")
+        O = torch.empty((B, H, D), dtype=dt, device=q3.device)
+        L = torch.empty((B, H), dtype=torch.float32, device=q3.device)
+        s = float(D) ** -0.5 if scale is None else float(scale)
+        _lib.check(lib.b2a_decode_paged(
+            qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), bt.data_ptr(), kl.data_ptr(),
+            o_part.data_ptr(), l_part.data_ptr(), O.data_ptr(), L.data_ptr(),
+            B, H, Hkv, D, page, max_pages, P, int(pages_per_split), _DT[dt], s,
+            _stream(q3.device)))
+    if had_len:
+        return [O.unsqueeze(2), L.unsqueeze(2)]
+    return [O, L]
+
+
+def device_error_flags() -> int:
+    """Read and clear the current device's kernel error word (synchronises)."""
+    import ctypes
+    lib = _lib.load()
+    v = ctypes.c_uint32(0)
+    _lib.check(lib.b2a_device_error(ctypes.byref(v)))
+    return int(v.value)
+
+
+def default_scale(D: int) -> float:
+    return 1.0 / math.sqrt(D)

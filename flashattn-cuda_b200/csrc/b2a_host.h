@@ -1,0 +1,57 @@
+// b2a_host.h -- host-side helpers shared by the kernels' launchers:
+// thread-local error messages, device checks and TMA tensor-map encoding.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/b200attn.h"
+
+namespace b2a {
+
+constexpr int kMaxDevices = 64;
+
+// Record `msg` as this thread's last error and return `status`.
+int set_error(int status, const char* msg);
+// Record a CUDA runtime failure ("<what>: <cuda error string>").
+int set_cuda_error(cudaError_t e, const char* what);
+
+// 3-D tiled tensor map over a contiguous [outer, rows, inner] array of 2-byte
+// elements: dims {inner, rows, outer}, box {box_inner, box_rows, 1}.  Rows past
+// `rows` (per outer index) read as zero.
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner,
+                 uint64_t rows, uint64_t outer, uint32_t box_inner, uint32_t box_rows,
+                 bool swizzle128);
+// 2-D tiled tensor map over a contiguous [rows, inner] array of 2-byte elements.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner,
+                 uint64_t rows, uint32_t box_inner, uint32_t box_rows, bool swizzle128);
+
+// Read-and-clear of each translation unit's device error word.
+int take_error_flags_prefill(uint32_t* flags);
+int take_error_flags_decode(uint32_t* flags);
+
+// Defines take_error_flags_<unit>() for the unit that expands it.
+#define B2A_DEFINE_ERROR_READER(unit)                                          \
+  int take_error_flags_##unit(uint32_t* flags) {                              \
+    uint32_t v = 0, zero = 0;                                                 \
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_error_flags, sizeof v);        \
+    if (e != cudaSuccess) return set_cuda_error(e, "read device error word"); \
+    e = cudaMemcpyToSymbol(g_error_flags, &zero, sizeof zero);                \
+    if (e != cudaSuccess) return set_cuda_error(e, "clear device error word");\
+    *flags |= v;                                                              \
+    return B2A_OK;                                                            \
+  }
+
+// Kernel dispatchers (defined next to their kernels).
+int prefill_dispatch(const void* q, const void* k, const void* v, void* o, float* lse, int B,
+                     int H, int Hkv, int N, int D, int dtype, int causal, float scale,
+                     cudaStream_t stream);
+int decode_dispatch(const void* q, const void* k, const void* v, const int32_t* block_table,
+                    const int32_t* kv_lens, float* o_part, float* l_part, int B, int H, int Hkv,
+                    int Lkv, int D, int splits, int tokens_per_split, int page_size, int max_pages,
+                    int num_pages, int dtype, float scale, cudaStream_t stream);
+int combine_dispatch(const float* o_part, const float* l_part, void* o, float* lse, int B, int H,
+                     int splits, int D, int dtype, const int32_t* kv_lens, int tokens_per_split,
+                     cudaStream_t stream);
+
+}  // namespace b2a

@@ -1,0 +1,118 @@
+/*
+ * b200attn.h -- C ABI of libb200attn.so, the B200 (sm_100a) attention library.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t passed
+ * as `void*`; nothing here names a torch or pybind type.  All buffers are owned
+ * by the caller (no allocation, no ownership transfer).  Calls are asynchronous
+ * on `stream` and return a status; a non-OK status leaves a human-readable
+ * message in b2a_last_error() (thread-local).
+ *
+ * Layouts (row-major, contiguous, element strides implied by the shape):
+ *   prefill    Q,O [B,H,N,D]; K,V [B,Hkv,N,D]; lse [B,H,N] fp32 (natural log)
+ *   decode     q,o [B,H,D] (query length 1); K,V [B,Hkv,Lkv,D]
+ *   partials   o_part [B,H,S,D] fp32 (each split normalised by its own sum),
+ *              l_part [B,H,S] fp32 (natural-log sum of exp over the split)
+ *   paged      k_pool,v_pool [P,Hkv,page_size,D]; block_table int32
+ *              [B,max_pages]; kv_lens int32 [B]
+ *
+ * Reference interface being replaced (Bias92/flashattn-cuda):
+ *   cuda/flash_attn_fa3_db_full.cu:349-403  fa3db_full_forward_impl
+ *   cuda/flash_attn_fa3_db_full.cu:405-418  forward / forward_only bindings
+ * The decode entry points have no function in the reference; they follow the
+ * same conventions (fp32 natural-log L, scale D^-0.5 by default).
+ */
+#ifndef B200ATTN_H_
+#define B200ATTN_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  B2A_OK = 0,
+  B2A_ERR_INVALID_ARG = 1,   /* bad shape / null pointer / out-of-range size   */
+  B2A_ERR_UNSUPPORTED = 2,   /* dtype, head dim or group size not built        */
+  B2A_ERR_MISALIGNED = 3,    /* a pointer is not 16-byte aligned (TMA rule)     */
+  B2A_ERR_CUDA = 4,          /* a CUDA runtime/driver call failed               */
+  B2A_ERR_TIMEOUT = 5,       /* a device-side bounded wait gave up             */
+  B2A_ERR_NO_DEVICE = 6      /* no sm_100 device is current                     */
+} b2a_status;
+
+typedef enum { B2A_F16 = 0, B2A_BF16 = 1 } b2a_dtype;
+
+/* Human-readable name of a status code. */
+const char* b2a_status_string(int status);
+/* Message of the last failing call on this thread ("" if none). */
+const char* b2a_last_error(void);
+/* Library version, e.g. "0.1.0". */
+const char* b2a_version(void);
+
+/*
+ * Prefill forward: O = softmax(Q K^T * scale [+ causal mask]) V and, when
+ * lse != NULL, L = logsumexp of the scaled scores per query row.
+ * lse == NULL is the O-only path (reference forward_only); O is bitwise equal
+ * between the two paths.  H % Hkv == 0 (Hkv == H is the reference's case).
+ * D in {64, 128}; dtype f16 or bf16 (the reference casts everything to f16).
+ * Replaces: cuda/flash_attn_fa3_db_full.cu:349-403 (fa3db_full_forward_impl)
+ * and the kernel fa3db_full_fwd_kernel (same file, 87-344).
+ */
+int b2a_prefill_fwd(const void* q, const void* k, const void* v, void* o,
+                    float* lse, int B, int H, int Hkv, int N, int D,
+                    int dtype, int causal, float scale, void* stream);
+
+/*
+ * Split-KV decode, first stage: for each (batch, query head, split) the
+ * softmax-normalised partial output and its natural-log sum of exp.  The KV
+ * sequence of length Lkv is cut into `splits` chunks of ceil(Lkv/splits)
+ * tokens; empty chunks write l = -inf, o = 0.  GQA group G = H/Hkv in
+ * {1,2,4,8}; D in {64,128}.  No counterpart in the reference (new entry point
+ * in the style of cuda/flash_attn_fa3_db_full.cu:405-408).
+ */
+int b2a_decode_splitkv(const void* q, const void* k, const void* v,
+                       float* o_part, float* l_part, int B, int H, int Hkv,
+                       int Lkv, int D, int splits, int dtype, float scale,
+                       void* stream);
+
+/*
+ * LSE-weighted combine of split partials: L = log sum_s exp(l_s),
+ * O = sum_s exp(l_s - L) * o_s, written as dtype O [B,H,D] and fp32 lse [B,H]
+ * (lse may be NULL).  The identity is the online-softmax rescale of
+ * cuda/flash_attn_fa3_db_full.cu:261-284 and :340 applied across splits.
+ */
+int b2a_decode_combine(const float* o_part, const float* l_part, void* o,
+                       float* lse, int B, int H, int splits, int D, int dtype,
+                       void* stream);
+
+/*
+ * Paged decode: as split-KV decode, but token t of sequence b lives in page
+ * block_table[b, t / page_size] at slot t % page_size of k_pool/v_pool
+ * ([P,Hkv,page_size,D]).  Sequence b has kv_lens[b] >= 1 tokens.  Each split
+ * covers `pages_per_split` pages; o_part/l_part are scratch sized
+ * [B,H,ceil(max_pages/pages_per_split),D] and [B,H,ceil(...)] that the caller
+ * provides.  num_pages is the pool size P; a block-table entry outside
+ * [0, P) sets bit 1 of the device error word and reads page 0 instead.
+ * Writes O [B,H,D] (dtype) and lse [B,H] (may be NULL).  page_size in
+ * {16, 32, 64}; pages_per_split * page_size a multiple of 64 and
+ * pages_per_split <= 256.  No counterpart in the reference.
+ */
+int b2a_decode_paged(const void* q, const void* k_pool, const void* v_pool,
+                     const int32_t* block_table, const int32_t* kv_lens,
+                     float* o_part, float* l_part, void* o, float* lse, int B,
+                     int H, int Hkv, int D, int page_size, int max_pages,
+                     int num_pages, int pages_per_split, int dtype, float scale,
+                     void* stream);
+
+/*
+ * Device error word written by the kernels (bit 0: a bounded pipeline wait
+ * timed out; bit 1: a paged-decode block-table entry was out of range).  Reads and clears the word of the current device; this
+ * call synchronises the device.  *flags receives the word.
+ */
+int b2a_device_error(uint32_t* flags);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200ATTN_H_ */

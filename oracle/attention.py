@@ -1,0 +1,167 @@
+"""CPU oracle for the attention hot path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference
+arm may import this module, and only as the checker or the timed CPU
+baseline.  The product path (b200attn) never calls it and has no CPU fallback.
+
+Every function restates, in numpy, the reference's naive attention
+(ref/naive_attn.py:10-38):
+
+    S = Q K^T * D^-0.5;  P = softmax(S);  O = P V;  L = logsumexp(S)
+
+with the extensions the B200 library adds (causal mask, GQA head sharing,
+explicit scale, decode with query length 1, split-KV partials and their
+LSE-weighted combine, paged-KV gather).  Arithmetic is float64 by default so
+that the oracle's own rounding is far below the tolerances under test; pass
+dtype=np.float32 to reproduce the reference's fp32 evaluation.
+
+Pinning: tests/test_oracle.py checks this module against golden vectors that
+tests/golden/make_golden.py produced by running the reference's own
+ref/naive_attn.py (torch, CPU) on seeded inputs, and against the reference
+tests' shape grid (tests/test_fa3_db_full.py:58-75).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def _kv_head(h: int, H: int, Hkv: int) -> int:
+    """Query head h reads KV head h // (H / Hkv) (GQA; identity when Hkv == H)."""
+    return h // (H // Hkv)
+
+
+def attention_head(q, k, v, scale, causal=False, row_offset=0, dtype=np.float64):
+    """One head: q [M, D] (query rows row_offset..row_offset+M-1), k/v [N, D].
+
+    Returns (O [M, D], L [M]).  Restates ref/naive_attn.py:27-36 for one
+    (b, h) slice; the causal mask keeps key j <= query row i.
+    """
+    q = np.asarray(q, dtype=dtype)
+    k = np.asarray(k, dtype=dtype)
+    v = np.asarray(v, dtype=dtype)
+    s = (q @ k.T) * dtype(scale)                     # S = Q K^T * scale   (:27)
+    if causal:
+        rows = np.arange(q.shape[0])[:, None] + row_offset
+        cols = np.arange(k.shape[0])[None, :]
+        s = np.where(cols <= rows, s, -np.inf)
+    m = s.max(axis=-1, keepdims=True)
+    e = np.exp(s - m)
+    z = e.sum(axis=-1, keepdims=True)
+    p = e / z                                        # P = softmax(S)      (:30)
+    o = p @ v                                        # O = P V             (:33)
+    lse = (m + np.log(z))[:, 0]                      # L = logsumexp(S)    (:36)
+    return o, lse
+
+
+def naive_attention(Q, K, V, scale=None, causal=False, dtype=np.float64):
+    """Q [B,H,N,D], K/V [B,Hkv,N,D] -> (O [B,H,N,D], L [B,H,N]) (ref/naive_attn.py:10-38)."""
+    Q = np.asarray(Q)
+    B, H, N, D = Q.shape
+    Hkv = K.shape[1]
+    scale = D ** -0.5 if scale is None else scale
+    O = np.empty((B, H, N, D), dtype=dtype)
+    L = np.empty((B, H, N), dtype=dtype)
+    for b in range(B):
+        for h in range(H):
+            hk = _kv_head(h, H, Hkv)
+            O[b, h], L[b, h] = attention_head(Q[b, h], K[b, hk], V[b, hk], scale, causal,
+                                              0, dtype)
+    return O, L
+
+
+def attention_rows(Q, K, V, b, h, rows, scale=None, causal=False, dtype=np.float64):
+    """O and L of selected query rows of head (b, h): for spot checks at large N."""
+    B, H, N, D = Q.shape
+    Hkv = K.shape[1]
+    scale = D ** -0.5 if scale is None else scale
+    hk = _kv_head(h, H, Hkv)
+    rows = np.asarray(rows)
+    outs_o, outs_l = [], []
+    for r in rows:
+        kk = K[b, hk, : r + 1] if causal else K[b, hk]
+        vv = V[b, hk, : r + 1] if causal else V[b, hk]
+        o, l = attention_head(Q[b, h, r:r + 1], kk, vv, scale, False, 0, dtype)
+        outs_o.append(o[0])
+        outs_l.append(l[0])
+    return np.stack(outs_o), np.array(outs_l)
+
+
+# ------------------------------------------------------------------------ decode
+
+def decode(q, k, v, scale=None, dtype=np.float64):
+    """q [B,H,D], k/v [B,Hkv,Lkv,D] -> (O [B,H,D], L [B,H]): attention of one query row."""
+    B, H, D = q.shape
+    Hkv = k.shape[1]
+    scale = D ** -0.5 if scale is None else scale
+    O = np.empty((B, H, D), dtype=dtype)
+    L = np.empty((B, H), dtype=dtype)
+    for b in range(B):
+        for h in range(H):
+            hk = _kv_head(h, H, Hkv)
+            o, l = attention_head(q[b, h][None], k[b, hk], v[b, hk], scale, False, 0, dtype)
+            O[b, h], L[b, h] = o[0], l[0]
+    return O, L
+
+
+def decode_splitkv_partials(q, k, v, splits, scale=None, dtype=np.float64):
+    """Per-split partials: (o_part [B,H,S,D], l_part [B,H,S]).
+
+    Split s covers tokens [s*c, min(Lkv, (s+1)*c)) with c = ceil(Lkv/S); o is the
+    softmax-normalised output over the split, l its natural-log sum of exp; an
+    empty split has l = -inf and o = 0.
+    """
+    B, H, D = q.shape
+    Hkv, Lkv = k.shape[1], k.shape[2]
+    scale = D ** -0.5 if scale is None else scale
+    c = -(-Lkv // splits)
+    o_part = np.zeros((B, H, splits, D), dtype=dtype)
+    l_part = np.full((B, H, splits), -np.inf, dtype=dtype)
+    for s in range(splits):
+        t0, t1 = s * c, min(Lkv, (s + 1) * c)
+        if t0 >= t1:
+            continue
+        o, l = decode(q, k[:, :, t0:t1], v[:, :, t0:t1], scale, dtype)
+        o_part[:, :, s], l_part[:, :, s] = o, l
+    return o_part, l_part
+
+
+def combine(o_part, l_part, dtype=np.float64):
+    """L = log sum_s exp(l_s);  O = sum_s exp(l_s - L) o_s  (online-softmax rescale,
+    cuda/flash_attn_fa3_db_full.cu:261-284 and :340, applied across splits)."""
+    o_part = np.asarray(o_part, dtype=dtype)
+    l_part = np.asarray(l_part, dtype=dtype)
+    M = l_part.max(axis=-1, keepdims=True)
+    w = np.where(np.isneginf(l_part), 0.0, np.exp(l_part - M))
+    Z = w.sum(axis=-1, keepdims=True)
+    O = (w[..., None] * o_part).sum(axis=-2) / Z
+    L = (M + np.log(Z))[..., 0]
+    return O, L
+
+
+def paged_gather(pool, block_table_row, length):
+    """Contiguous [Hkv, length, D] view of one sequence from a [P, Hkv, page, D] pool."""
+    page = pool.shape[2]
+    npages = -(-length // page)
+    pages = [pool[block_table_row[i]] for i in range(npages)]      # each [Hkv, page, D]
+    return np.concatenate(pages, axis=1)[:, :length]
+
+
+def decode_paged(q, k_pool, v_pool, block_table, kv_lens, scale=None, dtype=np.float64):
+    """Paged decode: token t of sequence b is slot t % page of page block_table[b, t // page]."""
+    B, H, D = q.shape
+    O = np.empty((B, H, D), dtype=dtype)
+    L = np.empty((B, H), dtype=dtype)
+    for b in range(B):
+        kb = paged_gather(k_pool, block_table[b], int(kv_lens[b]))[None]
+        vb = paged_gather(v_pool, block_table[b], int(kv_lens[b]))[None]
+        o, l = decode(q[b:b + 1], kb, vb, scale, dtype)
+        O[b], L[b] = o[0], l[0]
+    return O, L
+
+
+# ----------------------------------------------------------------- seeded inputs
+
+def seeded_normal(shape, seed, amp=1.0):
+    """N(0,1)*amp float32 values from a seeded generator (device-independent bits)."""
+    rng = np.random.default_rng(seed)
+    return (rng.standard_normal(shape, dtype=np.float32) * np.float32(amp))

@@ -1,0 +1,158 @@
+"""Prefill forward on the B200: parity with the oracle and with golden vectors
+from the reference's own naive attention, over the reference test grid
+(tests/test_fa3_db_full.py:58-75) and the north-star configurations."""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_parity, golden_files, load_golden
+from oracle import attention as ora
+
+pytestmark = pytest.mark.gpu
+
+TDT = {"float16": torch.float16, "bfloat16": torch.bfloat16}
+
+
+@pytest.fixture(scope="module")
+def b2a():
+    assert torch.cuda.is_available(), "gpu tests need a CUDA device"
+    import b200attn
+    return b200attn
+
+
+def dev(a, dtype):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dtype).cuda()
+
+
+def host(t):
+    return t.float().cpu().numpy()
+
+
+def seeded(shape_q, shape_kv, seed, amp, dtype):
+    """Seeded CPU inputs (identical bits on every device) rounded to `dtype`."""
+    q = dev(ora.seeded_normal(shape_q, seed, amp), dtype)
+    k = dev(ora.seeded_normal(shape_kv, seed + 1, amp), dtype)
+    v = dev(ora.seeded_normal(shape_kv, seed + 2, amp), dtype)
+    return q, k, v
+
+
+@pytest.mark.parametrize("path", golden_files("prefill"), ids=lambda p: os.path.basename(p)[:-4])
+def test_golden_prefill(b2a, path):
+    g = load_golden(path)
+    dt = TDT[g["dtype"]]
+    q, k, v = dev(g["q"], dt), dev(g["k"], dt), dev(g["v"], dt)
+    O, L = b2a.forward(q, k, v)
+    assert O.dtype == dt and L.dtype == torch.float32
+    assert_parity(O, L, g["O"], g["L"], g["dtype"], g["amp"], g["name"])
+    O2 = b2a.forward_only(q, k, v)
+    assert torch.equal(O2, O), "forward_only O must be bitwise equal to forward's O"
+
+
+REF_GRID = [
+    (1, 1, 64), (1, 1, 128), (2, 8, 512), (1, 1, 1024), (1, 1, 2048), (1, 1, 4096),
+    (1, 1, 1), (1, 1, 2), (1, 1, 7), (1, 1, 31), (1, 1, 33), (1, 1, 63), (1, 1, 127),
+    (1, 1, 4095), (2, 4, 256),
+]
+
+
+@pytest.mark.parametrize("B,H,N", REF_GRID, ids=lambda x: str(x))
+def test_reference_grid_fp32_inputs(b2a, B, H, N):
+    # fp32 inputs are cast to fp16 like the reference (cuda/flash_attn_fa3_db_full.cu:366)
+    q32 = torch.from_numpy(ora.seeded_normal((B, H, N, 64), 42)).cuda()
+    k32 = torch.from_numpy(ora.seeded_normal((B, H, N, 64), 43)).cuda()
+    v32 = torch.from_numpy(ora.seeded_normal((B, H, N, 64), 44)).cuda()
+    O, L = b2a.forward(q32, k32, v32)
+    assert O.dtype == torch.float16
+    Or, Lr = ora.naive_attention(host(q32.half()), host(k32.half()), host(v32.half()))
+    assert_parity(O, L, Or, Lr, "float16", 1.0, f"{B},{H},{N}")
+    assert torch.equal(b2a.forward_only(q32, k32, v32), O)
+
+
+@pytest.mark.parametrize("N,amp", [(2048, 16.0), (4095, 16.0), (1024, 8.0)])
+def test_large_logit_stress(b2a, N, amp):
+    q, k, v = seeded((1, 1, N, 64), (1, 1, N, 64), 7, amp, torch.float16)
+    O, L = b2a.forward(q, k, v)
+    Or, Lr = ora.naive_attention(host(q), host(k), host(v))
+    assert_parity(O, L, Or, Lr, "float16", amp, f"N={N} amp={amp}")
+
+
+VARIANTS = [
+    # B, H, Hkv, N, D, dtype, causal
+    (1, 2, 2, 300, 128, torch.float16, False),
+    (1, 2, 2, 300, 128, torch.bfloat16, False),
+    (2, 2, 2, 257, 64, torch.bfloat16, True),
+    (1, 4, 4, 640, 128, torch.bfloat16, True),
+    (1, 3, 3, 129, 64, torch.float16, True),
+    (1, 8, 2, 384, 128, torch.float16, False),   # GQA group 4
+    (2, 4, 1, 200, 64, torch.bfloat16, True),    # MQA
+    (1, 1, 1, 1, 128, torch.bfloat16, True),
+]
+
+
+@pytest.mark.parametrize("B,H,Hkv,N,D,dt,causal", VARIANTS, ids=lambda x: str(x))
+def test_variants_vs_oracle(b2a, B, H, Hkv, N, D, dt, causal):
+    q, k, v = seeded((B, H, N, D), (B, Hkv, N, D), 100 + N, 1.0, dt)
+    O, L = b2a.forward(q, k, v, causal=causal)
+    Or, Lr = ora.naive_attention(host(q), host(k), host(v), causal=causal)
+    name = "bfloat16" if dt == torch.bfloat16 else "float16"
+    assert_parity(O, L, Or, Lr, name, 1.0, f"{B},{H},{Hkv},{N},{D},{causal}")
+    assert torch.equal(b2a.forward_only(q, k, v, causal=causal), O)
+
+
+def test_explicit_scale(b2a):
+    q, k, v = seeded((1, 2, 200, 64), (1, 2, 200, 64), 5, 1.0, torch.float16)
+    O, L = b2a.forward(q, k, v, scale=0.3)
+    Or, Lr = ora.naive_attention(host(q), host(k), host(v), scale=0.3)
+    assert_parity(O, L, Or, Lr, "float16")
+
+
+@pytest.mark.parametrize("cfg", ["config1", "config2"])
+def test_headline_configs_full_size(b2a, cfg):
+    N = 1024 if cfg == "config1" else 4096
+    q, k, v = seeded((1, 8, N, 64), (1, 8, N, 64), 0, 1.0, torch.float16)
+    O, L = b2a.forward(q, k, v)
+    Or, Lr = ora.naive_attention(host(q), host(k), host(v))
+    assert_parity(O, L, Or, Lr, "float16", 1.0, cfg)
+
+
+def test_config3_causal_bf16_sampled(b2a):
+    """Config 3 at full size ([4,32,8192,128] bf16 causal): oracle rows sampled
+    from several heads, plus the size-independent row-0 identity O[0] = V[0]."""
+    B, H, N, D = 4, 32, 8192, 128
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q = torch.randn(B, H, N, D, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(B, H, N, D, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B, H, N, D, device="cuda", generator=g).to(torch.bfloat16)
+    O, L = b2a.forward(q, k, v, causal=True)
+    torch.cuda.synchronize()
+    assert torch.isfinite(O).all() and torch.isfinite(L).all()
+    # row 0 attends to key 0 only: O = V[0] exactly, L = q0.k0 * scale
+    assert torch.equal(O[:, :, 0], v[:, :, 0])
+    rows = [0, 1, 127, 128, 129, 4095, 4096, 8190, 8191]
+    for b, h in [(0, 0), (1, 17), (3, 31)]:
+        qh, kh, vh = host(q[b:b + 1, h:h + 1]), host(k[b:b + 1, h:h + 1]), host(v[b:b + 1, h:h + 1])
+        Or, Lr = ora.attention_rows(qh, kh, vh, 0, 0, rows, scale=D ** -0.5, causal=True)
+        assert_parity(O[b, h, rows], L[b, h, rows], Or, Lr, "bfloat16", 1.0, f"b{b}h{h}")
+
+
+def test_misaligned_pointer_rejected(b2a):
+    from b200attn import _lib
+    lib = _lib.load()
+    buf = torch.zeros(2 * 64 * 64 + 8, dtype=torch.float16, device="cuda")
+    base = buf.data_ptr() + 2  # 2-byte offset: not 16-byte aligned
+    rc = lib.b2a_prefill_fwd(base, base, base, base, None, 1, 1, 1, 64, 64, 0, 0, 0.125,
+                             torch.cuda.current_stream().cuda_stream)
+    assert rc == 3
+    assert b"16-byte aligned" in lib.b2a_last_error()
+
+
+def test_no_device_errors_recorded(b2a):
+    q, k, v = seeded((1, 2, 512, 128), (1, 2, 512, 128), 9, 1.0, torch.bfloat16)
+    b2a.forward(q, k, v, causal=True)
+    torch.cuda.synchronize()
+    assert b2a.device_error_flags() == 0
