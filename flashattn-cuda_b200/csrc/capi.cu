@@ -170,7 +170,7 @@ int b2a_prefill_fwd(const void* q, const void* k, const void* v, void* o, float*
   if (B <= 0 || H <= 0 || Hkv <= 0) return set_error(B2A_ERR_INVALID_ARG, "B, H and Hkv must be > 0");
   if (H % Hkv != 0) return set_error(B2A_ERR_INVALID_ARG, "H must be a multiple of Hkv");
   if ((int64_t)B * H > 0x7fffffff) return set_error(B2A_ERR_INVALID_ARG, "B*H too large");
-  if ((N + 127) / 128 > 65535) return set_error(B2A_ERR_INVALID_ARG, "N too large (grid.y limit)");
+  if ((N + 255) / 256 > 65535) return set_error(B2A_ERR_INVALID_ARG, "N too large (grid.y limit)");
   if (!(scale > 0.f)) return set_error(B2A_ERR_INVALID_ARG, "scale must be > 0");
   B2A_TRY(check_device_ptr(q, "Q"));
   B2A_TRY(check_device_ptr(k, "K"));

@@ -4,25 +4,26 @@
 // query row, the computation of fa3db_full_fwd_kernel in the reference
 // (cuda/flash_attn_fa3_db_full.cu:87-344), re-designed for Blackwell:
 //
-//   * one CTA per (128 query rows, query head); grid.y walks query tiles from
-//     the last (heaviest under the causal mask) to the first;
-//   * warp 4  (TMA producer): Q once, then K_j / V_j tiles into a ring of
-//     kStages shared-memory stages with 128-byte swizzle (3-D tensor maps
-//     {D, N, B*Hkv}, so rows >= N read as zero);
-//   * warp 5  (MMA issuer, TMEM owner): S_j = Q K_j^T (M=128, N=128, K=D) into
-//     one of two TMEM S buffers, and O += P_j V_j (M=128, N=D, K=128) into the
-//     TMEM O accumulator; completion is signalled by tcgen05.commit;
-//   * warps 0-3 (softmax + correction + epilogue): thread r owns query row r =
-//     TMEM lane r.  It loads its S row, applies the tail / causal mask, keeps
-//     the running max in the log2 domain and rescales O in TMEM only when the
-//     max grows by more than kRescaleThreshold (the reference rescales every
-//     tile, cuda/flash_attn_fa3_db_full.cu:258-300), writes P = exp2(S - m) in
-//     the input dtype into a swizzled shared-memory tile for the PV UMMA, and
-//     finally normalises O by the row sum and writes O and L
-//     (L = m ln2 + ln l, cuda/flash_attn_fa3_db_full.cu:340).
+//   * one CTA per (256 query rows = two 128-row Q tiles, query head); grid.y
+//     walks query blocks from the last (heaviest under a causal mask) down;
+//   * warp 8 (TMA producer): Q0/Q1 once, then K_j / V_j tiles (128 keys) into
+//     a ring of kStages shared-memory stages, 128-byte swizzled (3-D tensor
+//     maps {D, N, B*Hkv}: rows >= N read as zero);
+//   * warp 9 (MMA issuer, TMEM owner): S_t = Q_t K_j^T (SS UMMA, M=128 N=128
+//     K=D) into TMEM S_t, and O_t += P_t V_j (TS UMMA: P_t read from TMEM,
+//     V_j from shared memory, M=128 N=D K=128) into TMEM O_t;
+//   * warps 0-3 / 4-7 (softmax warpgroups for Q tile 0 / 1): thread r owns
+//     query row r = TMEM lane r.  It loads its S row, applies the tail /
+//     causal mask, keeps the running max in the log2 domain, rescales O_t in
+//     TMEM only when the max grows by more than kRescaleThreshold (the
+//     reference rescales every tile, cuda/flash_attn_fa3_db_full.cu:258-300),
+//     and writes P = exp2(S - m) as packed 16-bit pairs back over S_t in TMEM
+//     (the reference packs P into registers, :286-293).  At the end it
+//     normalises O_t by the row sum and writes O and L = m ln2 + ln l (:340).
 //
-// Because the S buffers are double-buffered, S_{j+1} runs on the tensor core
-// while the softmax warps work on S_j, and PV_j runs while they work on S_{j+1}.
+// The two Q tiles ping-pong: while one warpgroup runs its softmax the tensor
+// core runs the other tile's PV and next S, so the MUFU/FMA work of the
+// softmax and the UMMA work overlap.
 #include "sm100_ptx.cuh"
 #include "b2a_host.h"
 
@@ -30,30 +31,32 @@ namespace b2a {
 
 namespace prefill {
 
-constexpr int BM = 128;               // query rows per CTA (= UMMA M = TMEM lanes)
-constexpr int BN = 128;               // keys per KV tile (= UMMA N of S)
-constexpr int kThreads = 192;         // 4 softmax warps + producer + MMA
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr uint32_t kTmemCols = 512;   // S0 [0,128) S1 [128,256) O [256,256+D)
+constexpr int BM = 128;              // rows per Q tile (= UMMA M = TMEM lanes)
+constexpr int BN = 128;              // keys per KV tile (= UMMA N of S)
+constexpr int kQTiles = 2;           // Q tiles per CTA
+constexpr int kRowsPerCta = BM * kQTiles;
+constexpr int kThreads = 320;        // 2 softmax warpgroups + producer + MMA
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8
 
 template <int D>
 struct Cfg {
   static constexpr int kStages = (D == 64) ? 4 : 2;
   static constexpr int kBlocks = D / 64;  // 64-element (128-byte) column blocks per row
-  static constexpr uint32_t kQBytes = BM * D * 2;
+  static constexpr uint32_t kQBytes = BM * D * 2;  // one Q tile
   static constexpr uint32_t kKVBytes = BN * D * 2;
-  static constexpr uint32_t kPBytes = BM * BN * 2;
   static constexpr uint32_t kOffQ = 0;
-  static constexpr uint32_t kOffK = kOffQ + kQBytes;
+  static constexpr uint32_t kOffK = kOffQ + kQTiles * kQBytes;
   static constexpr uint32_t kOffV = kOffK + kStages * kKVBytes;
-  static constexpr uint32_t kOffP = kOffV + kStages * kKVBytes;
-  static constexpr uint32_t kOffBar = kOffP + kPBytes;
+  static constexpr uint32_t kOffBar = kOffV + kStages * kKVBytes;
+  // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2], pv_done[2]
   static constexpr int kNumBars = 1 + 3 * kStages + 6;
   static constexpr uint32_t kOffTmemSlot = kOffBar + 8 * kNumBars;
   static constexpr uint32_t kOffAbort = kOffTmemSlot + 8;
   static constexpr uint32_t kSmemBytes = kOffAbort + 8 + 1024;  // + alignment slack
+  static constexpr uint32_t kTmemO = 256;                         // O_t at kTmemO + t*D
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -80,16 +83,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sQ = sb + C::kOffQ;
   const uint32_t sK = sb + C::kOffK;
   const uint32_t sV = sb + C::kOffV;
-  const uint32_t sP = sb + C::kOffP;
   const uint32_t bar0 = sb + C::kOffBar;
-  auto BAR_Q = [&]() { return bar0; };
+  const uint32_t BAR_Q = bar0;
   auto BAR_KF = [&](int s) { return bar0 + 8u * (1 + s); };
   auto BAR_VF = [&](int s) { return bar0 + 8u * (1 + S + s); };
   auto BAR_KVE = [&](int s) { return bar0 + 8u * (1 + 2 * S + s); };
-  auto BAR_SF = [&](int b) { return bar0 + 8u * (1 + 3 * S + b); };
-  auto BAR_SE = [&](int b) { return bar0 + 8u * (3 + 3 * S + b); };
-  const uint32_t BAR_PF = bar0 + 8u * (5 + 3 * S);
-  const uint32_t BAR_PVD = bar0 + 8u * (6 + 3 * S);
+  auto BAR_SF = [&](int t) { return bar0 + 8u * (1 + 3 * S + t); };
+  auto BAR_PF = [&](int t) { return bar0 + 8u * (3 + 3 * S + t); };
+  auto BAR_PVD = [&](int t) { return bar0 + 8u * (5 + 3 * S + t); };
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sp + C::kOffTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sp + C::kOffAbort);
 
@@ -97,17 +98,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int bh = blockIdx.x;
   const int bhk = (bh / H) * (H / group) + (bh % H) / group;  // KV head of this query head
-  const int qt = (int)gridDim.y - 1 - (int)blockIdx.y;
-  const int q0 = qt * BM;
+  const int qb = (int)gridDim.y - 1 - (int)blockIdx.y;
+  const int q0 = qb * kRowsPerCta;
   const int nkv_all = (N + BN - 1) / BN;
-  const int nkv = CAUSAL ? min(nkv_all, (q0 + BM + BN - 1) / BN) : nkv_all;
+  // KV tiles Q tile t needs (t = 0, 1); the loop runs to the larger one
+  int nkv_t[kQTiles];
+#pragma unroll
+  for (int t = 0; t < kQTiles; ++t)
+    nkv_t[t] = CAUSAL ? min(nkv_all, (q0 + (t + 1) * BM + BN - 1) / BN) : nkv_all;
+  const int nkv = nkv_t[kQTiles - 1];
 
   if (warp == kProducerWarp && lane == 0) {
-    // s_empty / p_full collect one arrival per softmax warp, the rest one
-    // arrival (expect_tx from the producer or a tcgen05.commit)
     for (int i = 0; i < C::kNumBars; ++i) {
       const uint32_t bar = bar0 + 8u * i;
-      const bool per_warp = bar == BAR_SE(0) || bar == BAR_SE(1) || bar == BAR_PF;
+      // p_full collects one arrival per softmax warp, the rest one arrival
+      // (expect_tx from the producer or a tcgen05.commit)
+      const bool per_warp = bar == BAR_PF(0) || bar == BAR_PF(1);
       mbar_init(bar, per_warp ? 4u : 1u);
     }
     *abort_flag = 0;
@@ -128,10 +134,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(BAR_Q(), C::kQBytes);
+      mbar_arrive_expect_tx(BAR_Q, kQTiles * C::kQBytes);
 #pragma unroll
-      for (int c = 0; c < C::kBlocks; ++c)
-        tma_load_3d(sQ + c * (BM * 128), &tmQ, BAR_Q(), c * 64, q0, bh);
+      for (int t = 0; t < kQTiles; ++t)
+#pragma unroll
+        for (int c = 0; c < C::kBlocks; ++c)
+          tma_load_3d(sQ + t * C::kQBytes + c * (BM * 128), &tmQ, BAR_Q, c * 64, q0 + t * BM, bh);
       for (int j = 0; j < nkv; ++j) {
         const int st = j % S;
         if (j >= S && !mbar_wait(BAR_KVE(st), ((j / S) - 1) & 1, abort_flag)) break;
@@ -152,80 +160,96 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16(BM, BN, BF16, false, false);
       constexpr uint32_t idesc_pv = idesc_f16(BM, D, BF16, false, true);
-      const uint32_t t_o = tmem + 256;
-      bool ok = mbar_wait(BAR_Q(), 0, abort_flag);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % S, b = j & 1;
-        if (!mbar_wait(BAR_KF(st), (j / S) & 1, abort_flag)) return false;
-        if (j >= 2 && !mbar_wait(BAR_SE(b), ((j >> 1) - 1) & 1, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t k_base = sK + st * C::kKVBytes;
+      bool ok = mbar_wait(BAR_Q, 0, abort_flag);
+      auto issue_s = [&](int t, int j) {
+        const uint32_t q_base = sQ + t * C::kQBytes;
+        const uint32_t k_base = sK + (j % S) * C::kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint64_t ad = sdesc_sw128(sQ + off, 16, 1024);
-          const uint64_t bd = sdesc_sw128(k_base + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
-          umma_f16_ss(tmem + b * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          const uint64_t ad = sdesc_sw128(q_base + off, 16, 1024);
+          const uint64_t bd = sdesc_sw128(k_base + off, 16, 1024);
+          umma_f16_ss(tmem + t * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        umma_commit(BAR_SF(b));
-        return true;
+        umma_commit(BAR_SF(t));
       };
-      auto issue_pv = [&](int j) -> bool {
-        const int st = j % S;
-        if (!mbar_wait(BAR_VF(st), (j / S) & 1, abort_flag)) return false;
-        if (!mbar_wait(BAR_PF, j & 1, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t v_base = sV + st * C::kKVBytes;
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t v_base = sV + (j % S) * C::kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(sP + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(v_base + kk * 2048, BN * 128, 1024);
-          umma_f16_ss(t_o, ad, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + C::kTmemO + t * D, tmem + t * 128 + kk * 8, bd, idesc_pv,
+                      (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(BAR_PVD);
-        umma_commit(BAR_KVE(st));
-        return true;
+        umma_commit(BAR_PVD(t));
       };
-      if (ok) ok = issue_s(0);
+      if (ok) ok = mbar_wait(BAR_KF(0), 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
       for (int j = 0; ok && j < nkv; ++j) {
-        if (j + 1 < nkv) ok = issue_s(j + 1);
-        if (ok) ok = issue_pv(j);
+        const int st = j % S;
+        if (!mbar_wait(BAR_VF(st), (j / S) & 1, abort_flag)) { ok = false; break; }
+        bool k_next_ready = false;
+#pragma unroll
+        for (int t = 0; t < kQTiles; ++t) {
+          if (j >= nkv_t[t]) continue;
+          if (!mbar_wait(BAR_PF(t), j & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, j);
+          if (j + 1 < nkv_t[t]) {
+            if (!k_next_ready) {
+              if (!mbar_wait(BAR_KF((j + 1) % S), ((j + 1) / S) & 1, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              k_next_ready = true;
+            }
+            issue_s(t, j + 1);
+          }
+        }
+        umma_commit(BAR_KVE(st));  // K_j / V_j free once every MMA above has run
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax warps 0-3
-    const int row = threadIdx.x;  // 0..127 == TMEM lane
-    const int grow = q0 + row;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const uint32_t t_o = tmem + lane_base + 256;
+    // ------------------------------------------------------------ softmax warpgroups
+    const int t = warp >> 2;           // Q tile of this warpgroup
+    const int row = threadIdx.x & 127;  // TMEM lane
+    const int grow = q0 + t * BM + row;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + lane_base + t * 128;
+    const uint32_t t_o = tmem + lane_base + C::kTmemO + t * D;
+    const int my_nkv = nkv_t[t];
     float m_run = -INFINITY;  // running max of scaled scores, log2 units
     float l_run = 0.f;
     bool ok = true;
-    uint8_t* prow = sp + C::kOffP + row * 128;
 
-    for (int j = 0; j < nkv && ok; ++j) {
-      const int b = j & 1;
-      if (!mbar_wait(BAR_SF(b), (j >> 1) & 1, abort_flag)) { ok = false; break; }
+    for (int j = 0; j < my_nkv && ok; ++j) {
+      if (!mbar_wait(BAR_SF(t), j & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
       float s[BN];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tmem_ld32(tmem + lane_base + b * 128 + c * 32, s + c * 32);
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(t_s + c * 32, s + c * 32);
       tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR_SE(b));
 
       const int kv0 = j * BN;
-      const bool need_mask = (kv0 + BN > N) || (CAUSAL && kv0 + BN > q0);
+      const bool need_mask = (kv0 + BN > N) || (CAUSAL && kv0 + BN > q0 + t * BM);
       if (need_mask) {
-        const int lim = CAUSAL ? min(N, grow + 1) : N;  // first masked key
+        const int lim = (CAUSAL ? min(N, grow + 1) : N) - kv0;  // first masked column
 #pragma unroll
         for (int c = 0; c < BN; ++c)
-          if (kv0 + c >= lim) s[c] = -INFINITY;
+          if (c >= lim) s[c] = -INFINITY;
       }
-      float mx = s[0];
+      float mx8[8];
 #pragma unroll
-      for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
+      for (int i = 0; i < 8; ++i) mx8[i] = s[i];
+#pragma unroll
+      for (int c = 8; c < BN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_tile = mx * scale_log2;
       const float m_new = fmaxf(m_run, m_tile);
       const bool rescale = m_new > m_run + kRescaleThreshold;  // true on the first tile
@@ -235,56 +259,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_run = m_new;
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      float rs0 = 0.f, rs1 = 0.f;
+      float rs[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rs[i] = 0.f;
+      uint32_t pk[BN / 2];
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {
-        s[c] = ex2(fmaf(s[c], scale_log2, -m_use));
-        s[c + 1] = ex2(fmaf(s[c + 1], scale_log2, -m_use));
-        rs0 += s[c];
-        rs1 += s[c + 1];
+        const float p0 = ex2(fmaf(s[c], scale_log2, -m_use));
+        const float p1 = ex2(fmaf(s[c + 1], scale_log2, -m_use));
+        rs[(c >> 1) & 7] += p0 + p1;
+        pk[c >> 1] = pack2_u32<BF16>(p0, p1);
       }
-      l_run = l_run * alpha + (rs0 + rs1);
+      l_run = l_run * alpha + (((rs[0] + rs[1]) + (rs[2] + rs[3])) +
+                               ((rs[4] + rs[5]) + (rs[6] + rs[7])));
 
-      // O and the P tile are still in use by PV_{j-1}
-      if (j > 0) {
-        if (!mbar_wait(BAR_PVD, (j - 1) & 1, abort_flag)) { ok = false; break; }
+      // O_t is still being accumulated by PV_{j-1}; rescale it once that is done
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+        if (!mbar_wait(BAR_PVD(t), (j - 1) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            float o[32];
-            tmem_ld32(t_o + c * 32, o);
-            tmem_ld_wait();
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(t_o + c * 32, o);
+          tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(t_o + c * 32, o);
-          }
-          tmem_st_wait();
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(t_o + c * 32, o);
         }
       }
-      // P row -> K-major 128B-swizzled tile: 16-byte chunk k8 of a row goes to
-      // chunk (k8 ^ (row & 7)) of that row's 128-byte line.
-#pragma unroll
-      for (int blk = 0; blk < BN / 64; ++blk) {
-#pragma unroll
-        for (int k8 = 0; k8 < 8; ++k8) {
-          const float* pv = s + blk * 64 + k8 * 8;
-          uint4 w;
-          w.x = pack2_u32<BF16>(pv[0], pv[1]);
-          w.y = pack2_u32<BF16>(pv[2], pv[3]);
-          w.z = pack2_u32<BF16>(pv[4], pv[5]);
-          w.w = pack2_u32<BF16>(pv[6], pv[7]);
-          *reinterpret_cast<uint4*>(prow + blk * (BM * 128) + ((k8 ^ (row & 7)) << 4)) = w;
-        }
-      }
-      fence_proxy_async_smem();
+      // P over S_t: 128 16-bit values = 64 packed columns
+      tmem_st32u(t_s, pk);
+      tmem_st32u(t_s + 32, pk + 32);
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(BAR_PF);
+      if (lane == 0) mbar_arrive(BAR_PF(t));
     }
 
     // ---------------------------------------------------------- epilogue
-    if (ok && mbar_wait(BAR_PVD, (nkv - 1) & 1, abort_flag)) {
+    if (ok && mbar_wait(BAR_PVD(t), (my_nkv - 1) & 1, abort_flag)) {
       tc_fence_after();
       const float inv_l = 1.f / l_run;
       typename E::T* orow = reinterpret_cast<typename E::T*>(out) + ((size_t)bh * N + grow) * D;
@@ -347,7 +360,7 @@ static int launch_prefill(const void* q, const void* k, const void* v, void* o, 
   if (rc != B2A_OK) return rc;
   rc = make_tmap_3d(&tv, v, dt, D, N, (uint64_t)B * Hkv, 64, BN, true);
   if (rc != B2A_OK) return rc;
-  dim3 grid((unsigned)(B * H), (unsigned)((N + BM - 1) / BM));
+  dim3 grid((unsigned)(B * H), (unsigned)((N + kRowsPerCta - 1) / kRowsPerCta));
   const float scale_log2 = scale * 1.4426950408889634f;
   kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, o, lse, N, H, H / Hkv, scale_log2);
   cudaError_t e = cudaGetLastError();
