@@ -35,9 +35,17 @@ constexpr int BM = 128;              // rows per Q tile (= UMMA M = TMEM lanes)
 constexpr int BN = 128;              // keys per KV tile (= UMMA N of S)
 constexpr int kQTiles = 2;           // Q tiles per CTA
 constexpr int kRowsPerCta = BM * kQTiles;
-constexpr int kThreads = 320;        // 2 softmax warpgroups + producer + MMA
+constexpr int kThreads = 384;        // 2 softmax warpgroups + {producer, MMA, 2 idle}
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
+// Register split: launched at kLaunchRegs per thread (the most 12 warps can
+// have), the producer/MMA warpgroup gives registers to the softmax ones:
+// 128 * kRegsCtrl + 256 * kRegsSoftmax == 384 * kLaunchRegs.
+constexpr uint32_t kLaunchRegs = 168;
+constexpr uint32_t kRegsCtrl = 56;
+constexpr uint32_t kRegsSoftmax = 224;
+static_assert(128 * kRegsCtrl + 256 * kRegsSoftmax == kThreads * kLaunchRegs,
+              "register split must add up to the launch allocation");
 constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8
 
@@ -59,12 +67,6 @@ struct Cfg {
   static constexpr uint32_t kTmemO = 256;                         // O_t at kTmemO + t*D
 };
 
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 template <int D, bool BF16, bool CAUSAL>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -74,6 +76,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = Cfg<D>;
   using E = Elem<BF16>;
   constexpr int S = C::kStages;
+  // of every 8 consecutive (even, odd) score pairs, this many take the
+  // polynomial exp2 on the FMA pipe and the rest the MUFU ex2, so that the two
+  // pipes share the exponentials of a tile
+  constexpr int kPolyPairsPer8 = (D == 64) ? 3 : 2;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -128,93 +134,97 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(BAR_Q, kQTiles * C::kQBytes);
+  if (warp >= 8) {
+    setmaxnreg_dec<kRegsCtrl>();
+    if (warp == kProducerWarp) {
+      // ------------------------------------------------------------ producer
+      if (lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        mbar_arrive_expect_tx(BAR_Q, kQTiles * C::kQBytes);
 #pragma unroll
-      for (int t = 0; t < kQTiles; ++t)
+        for (int t = 0; t < kQTiles; ++t)
 #pragma unroll
-        for (int c = 0; c < C::kBlocks; ++c)
-          tma_load_3d(sQ + t * C::kQBytes + c * (BM * 128), &tmQ, BAR_Q, c * 64, q0 + t * BM, bh);
-      for (int j = 0; j < nkv; ++j) {
-        const int st = j % S;
-        if (j >= S && !mbar_wait(BAR_KVE(st), ((j / S) - 1) & 1, abort_flag)) break;
-        const uint32_t k_dst = sK + st * C::kKVBytes;
-        const uint32_t v_dst = sV + st * C::kKVBytes;
-        mbar_arrive_expect_tx(BAR_KF(st), C::kKVBytes);
+          for (int c = 0; c < C::kBlocks; ++c)
+            tma_load_3d(sQ + t * C::kQBytes + c * (BM * 128), &tmQ, BAR_Q, c * 64, q0 + t * BM, bh);
+        for (int j = 0; j < nkv; ++j) {
+          const int st = j % S;
+          if (j >= S && !mbar_wait(BAR_KVE(st), ((j / S) - 1) & 1, abort_flag)) break;
+          const uint32_t k_dst = sK + st * C::kKVBytes;
+          const uint32_t v_dst = sV + st * C::kKVBytes;
+          mbar_arrive_expect_tx(BAR_KF(st), C::kKVBytes);
 #pragma unroll
-        for (int c = 0; c < C::kBlocks; ++c)
-          tma_load_3d(k_dst + c * (BN * 128), &tmK, BAR_KF(st), c * 64, j * BN, bhk);
-        mbar_arrive_expect_tx(BAR_VF(st), C::kKVBytes);
+          for (int c = 0; c < C::kBlocks; ++c)
+            tma_load_3d(k_dst + c * (BN * 128), &tmK, BAR_KF(st), c * 64, j * BN, bhk);
+          mbar_arrive_expect_tx(BAR_VF(st), C::kKVBytes);
 #pragma unroll
-        for (int c = 0; c < C::kBlocks; ++c)
-          tma_load_3d(v_dst + c * (BN * 128), &tmV, BAR_VF(st), c * 64, j * BN, bhk);
-      }
-    }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_qk = idesc_f16(BM, BN, BF16, false, false);
-      constexpr uint32_t idesc_pv = idesc_f16(BM, D, BF16, false, true);
-      bool ok = mbar_wait(BAR_Q, 0, abort_flag);
-      auto issue_s = [&](int t, int j) {
-        const uint32_t q_base = sQ + t * C::kQBytes;
-        const uint32_t k_base = sK + (j % S) * C::kKVBytes;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint64_t ad = sdesc_sw128(q_base + off, 16, 1024);
-          const uint64_t bd = sdesc_sw128(k_base + off, 16, 1024);
-          umma_f16_ss(tmem + t * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          for (int c = 0; c < C::kBlocks; ++c)
+            tma_load_3d(v_dst + c * (BN * 128), &tmV, BAR_VF(st), c * 64, j * BN, bhk);
         }
-        umma_commit(BAR_SF(t));
-      };
-      auto issue_pv = [&](int t, int j) {
-        const uint32_t v_base = sV + (j % S) * C::kKVBytes;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bd = sdesc_sw128(v_base + kk * 2048, BN * 128, 1024);
-          umma_f16_ts(tmem + C::kTmemO + t * D, tmem + t * 128 + kk * 8, bd, idesc_pv,
-                      (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(BAR_PVD(t));
-      };
-      if (ok) ok = mbar_wait(BAR_KF(0), 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
       }
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int st = j % S;
-        if (!mbar_wait(BAR_VF(st), (j / S) & 1, abort_flag)) { ok = false; break; }
-        bool k_next_ready = false;
+    } else if (warp == kMmaWarp) {
+      // ------------------------------------------------------------ MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc_qk = idesc_f16(BM, BN, BF16, false, false);
+        constexpr uint32_t idesc_pv = idesc_f16(BM, D, BF16, false, true);
+        bool ok = mbar_wait(BAR_Q, 0, abort_flag);
+        auto issue_s = [&](int t, int j) {
+          const uint32_t q_base = sQ + t * C::kQBytes;
+          const uint32_t k_base = sK + (j % S) * C::kKVBytes;
 #pragma unroll
-        for (int t = 0; t < kQTiles; ++t) {
-          if (j >= nkv_t[t]) continue;
-          if (!mbar_wait(BAR_PF(t), j & 1, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(t, j);
-          if (j + 1 < nkv_t[t]) {
-            if (!k_next_ready) {
-              if (!mbar_wait(BAR_KF((j + 1) % S), ((j + 1) / S) & 1, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              k_next_ready = true;
-            }
-            issue_s(t, j + 1);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+            const uint64_t ad = sdesc_sw128(q_base + off, 16, 1024);
+            const uint64_t bd = sdesc_sw128(k_base + off, 16, 1024);
+            umma_f16_ss(tmem + t * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
           }
+          umma_commit(BAR_SF(t));
+        };
+        auto issue_pv = [&](int t, int j) {
+          const uint32_t v_base = sV + (j % S) * C::kKVBytes;
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t bd = sdesc_sw128(v_base + kk * 2048, BN * 128, 1024);
+            umma_f16_ts(tmem + C::kTmemO + t * D, tmem + t * 128 + kk * 8, bd, idesc_pv,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(BAR_PVD(t));
+        };
+        if (ok) ok = mbar_wait(BAR_KF(0), 0, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0, 0);
+          issue_s(1, 0);
         }
-        umma_commit(BAR_KVE(st));  // K_j / V_j free once every MMA above has run
+        for (int j = 0; ok && j < nkv; ++j) {
+          const int st = j % S;
+          if (!mbar_wait(BAR_VF(st), (j / S) & 1, abort_flag)) { ok = false; break; }
+          bool k_next_ready = false;
+#pragma unroll
+          for (int t = 0; t < kQTiles; ++t) {
+            if (j >= nkv_t[t]) continue;
+            if (!mbar_wait(BAR_PF(t), j & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(t, j);
+            if (j + 1 < nkv_t[t]) {
+              if (!k_next_ready) {
+                if (!mbar_wait(BAR_KF((j + 1) % S), ((j + 1) / S) & 1, abort_flag)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                k_next_ready = true;
+              }
+              issue_s(t, j + 1);
+            }
+          }
+          umma_commit(BAR_KVE(st));  // K_j / V_j free once every MMA above has run
+        }
       }
     }
   } else {
+    setmaxnreg_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax warpgroups
     const int t = warp >> 2;           // Q tile of this warpgroup
     const int row = threadIdx.x & 127;  // TMEM lane
@@ -245,33 +255,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float mx8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = s[i];
+      for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(s[i], s[i + 8]);
 #pragma unroll
-      for (int c = 8; c < BN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      for (int c = 16; c < BN; c += 16)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = fmax3(mx8[i], s[c + i], s[c + 8 + i]);
+      const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                             fmaxf(mx8[6], mx8[7]));
       const float m_tile = mx * scale_log2;
       const float m_new = fmaxf(m_run, m_tile);
       const bool rescale = m_new > m_run + kRescaleThreshold;  // true on the first tile
       float alpha = 1.f;
       if (rescale) {
-        alpha = ex2(m_run - m_new);  // 0 when m_run == -inf
+        alpha = ex2_mufu(m_run - m_new);  // 0 when m_run == -inf
         m_run = m_new;
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      float rs[8];
+      const float2 sc2 = make_float2(scale_log2, scale_log2);
+      const float2 nm2 = make_float2(-m_use, -m_use);
+      float2 rs[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) rs[i] = 0.f;
+      for (int i = 0; i < 4; ++i) rs[i] = make_float2(0.f, 0.f);
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {
-        const float p0 = ex2(fmaf(s[c], scale_log2, -m_use));
-        const float p1 = ex2(fmaf(s[c + 1], scale_log2, -m_use));
-        rs[(c >> 1) & 7] += p0 + p1;
-        pk[c >> 1] = pack2_u32<BF16>(p0, p1);
+        const float2 x = ffma2(make_float2(s[c], s[c + 1]), sc2, nm2);
+        float2 p;
+        if (((c >> 1) & 7) < kPolyPairsPer8) {
+          p = exp2_poly2(x);  // FMA pipe
+        } else {
+          p.x = ex2_mufu(x.x);  // MUFU pipe
+          p.y = ex2_mufu(x.y);
+        }
+        rs[(c >> 1) & 3] = fadd2(rs[(c >> 1) & 3], p);
+        pk[c >> 1] = pack2_u32<BF16>(p.x, p.y);
       }
-      l_run = l_run * alpha + (((rs[0] + rs[1]) + (rs[2] + rs[3])) +
-                               ((rs[4] + rs[5]) + (rs[6] + rs[7])));
+      const float2 r01 = fadd2(fadd2(rs[0], rs[1]), fadd2(rs[2], rs[3]));
+      l_run = l_run * alpha + (r01.x + r01.y);
 
       // O_t is still being accumulated by PV_{j-1}; rescale it once that is done
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {

@@ -232,6 +232,76 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool a
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Per-warpgroup register re-allocation (all 128 threads of a warpgroup execute
+// it).  The increases of some warpgroups must be covered by the decreases of
+// the others within the block's launch allocation.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// ---------------------------------------------------------------------------
+// packed fp32 math (sm_100 f32x2 instructions) and exp2
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 A, B, C, D;\n\t"
+      "mov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\tmov.b64 C, {%6, %7};\n\t"
+      "fma.rn.f32x2 D, A, B, C;\n\tmov.b64 {%0, %1}, D;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 A, B, D;\n\t"
+      "mov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
+      "add.rn.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// MUFU ex2 (hardware approximation, flushes subnormal results to zero)
+__device__ __forceinline__ float ex2_mufu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// 2^x for a pair of x <= ~64 on the FMA/ALU pipes, so that part of a softmax's
+// exponentials can run beside the MUFU unit.  Method: Cody-Waite style range
+// reduction x = n + f with n = round(x) obtained by adding and subtracting
+// 1.5 * 2^23 (f in [-1/2, 1/2]); 2^f by a degree-4 polynomial whose
+// coefficients were fitted here to 2^f on [-1/2, 1/2] in relative error
+// (Chebyshev nodes, iteratively reweighted least squares toward equiripple;
+// max relative error 2.6e-6); 2^n applied by adding n to the exponent field.
+// Inputs below -126 are clamped to -126 (result ~1e-38, never a NaN).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  const float2 kShift = make_float2(12582912.f, 12582912.f);
+  const float2 kNegShift = make_float2(-12582912.f, -12582912.f);
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = fadd2(x, kShift);  // n in the low mantissa bits
+  const float2 n = fadd2(t, kNegShift);
+  const float2 f = fadd2(x, make_float2(-n.x, -n.y));
+  float2 p = ffma2(make_float2(0.009570101276040077f, 0.009570101276040077f), f,
+                   make_float2(0.05591785907745361f, 0.05591785907745361f));
+  p = ffma2(p, f, make_float2(0.240247443318367f, 0.240247443318367f));
+  p = ffma2(p, f, make_float2(0.6931217908859253f, 0.6931217908859253f));
+  p = ffma2(p, f, make_float2(0.9999992847442627f, 0.9999992847442627f));
+  p.x = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
+  p.y = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
+  return p;
+}
+
 // ---------------------------------------------------------------------------
 // element helpers
 // ---------------------------------------------------------------------------
