@@ -29,6 +29,8 @@ _SIGNATURES = {
     "b2a_decode_combine": (_c_int, [_vp] * 4 + [_c_int] * 5 + [_vp]),
     # q kp vp bt lens o_part l_part o lse | B H Hkv D page max_pages num_pages pps | dtype scale stream
     "b2a_decode_paged": (_c_int, [_vp] * 9 + [_c_int] * 8 + [_c_int, _c_float, _vp]),
+    # q kp vp bt lens o lse | B H Hkv D page max_pages num_pages pps | dtype scale stream
+    "b2a_decode_paged_noalloc": (_c_int, [_vp] * 7 + [_c_int] * 8 + [_c_int, _c_float, _vp]),
     "b2a_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint32)]),
 }
 

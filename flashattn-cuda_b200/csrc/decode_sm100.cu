@@ -18,6 +18,9 @@
 //     0..G-1 of the A operand), with the online softmax on the accumulator
 //     fragments;  the four warps' (m, l, o) states merge through shared memory
 //     at the end, and the CTA writes the split's normalised o and natural-log l.
+#include <cstdio>
+#include <mutex>
+
 #include "sm100_ptx.cuh"
 #include "b2a_host.h"
 
@@ -459,4 +462,70 @@ int combine_dispatch(const float* o_part, const float* l_part, void* o, float* l
   return B2A_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Scratch for b2a_decode_paged_noalloc.  Some callers cannot allocate device
+// memory at the point where they decode: an allocator-free serving runtime
+// that owns all of HBM up front, code running inside a memory pool that must
+// not grow, or a plugin host that forbids cudaMalloc on its request path.
+// For them the split partials live in this fixed array instead of a
+// caller-provided buffer.  Every GPU that loads the library holds it (16 MiB)
+// until the process exits.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchFloats = 4u * 1024u * 1024u;  // 16 MiB
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+// Device address of g_noalloc_scratch on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device with cudaGetSymbolAddress (with that device current) and cached.
+static int noalloc_scratch_ptr(float** out) {
+  static float* ptrs[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return set_error(B2A_ERR_INVALID_ARG, "device index too large");
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    ptrs[dev] = static_cast<float*>(p);
+  }
+  *out = ptrs[dev];
+  return B2A_OK;
+}
+
 }  // namespace b2a
+
+extern "C" int b2a_decode_paged_noalloc(const void* q, const void* k_pool, const void* v_pool,
+                                        const int32_t* block_table, const int32_t* kv_lens,
+                                        void* o, float* lse, int B, int H, int Hkv, int D,
+                                        int page_size, int max_pages, int num_pages,
+                                        int pages_per_split, int dtype, float scale,
+                                        void* stream) {
+  using namespace b2a;
+  if (B <= 0 || H <= 0 || D <= 0 || max_pages <= 0 || pages_per_split <= 0)
+    return set_error(B2A_ERR_INVALID_ARG,
+                     "B, H, D, max_pages and pages_per_split must be > 0");
+  const size_t splits = ((size_t)max_pages + pages_per_split - 1) / pages_per_split;
+  const size_t rows = (size_t)B * H * splits;
+  const size_t need = rows * (size_t)D + rows;
+  if (need > kNoAllocScratchFloats) {
+    char buf[256];
+    snprintf(buf, sizeof buf,
+             "decode_paged_noalloc: B*H*ceil(max_pages/pages_per_split)*(D+1) = %zu floats "
+             "exceeds the fixed scratch of %zu floats (16 MiB); use b2a_decode_paged with a "
+             "caller-provided scratch buffer or raise pages_per_split",
+             need, kNoAllocScratchFloats);
+    return set_error(B2A_ERR_INVALID_ARG, buf);
+  }
+  float* scratch = nullptr;
+  int rc = noalloc_scratch_ptr(&scratch);
+  if (rc != B2A_OK) return rc;
+  float* o_part = scratch;                       // [B, H, splits, D]
+  float* l_part = scratch + rows * (size_t)D;    // [B, H, splits]; 16-byte aligned (D % 4 == 0)
+  return b2a_decode_paged(q, k_pool, v_pool, block_table, kv_lens, o_part, l_part, o, lse, B, H,
+                          Hkv, D, page_size, max_pages, num_pages, pages_per_split, dtype, scale,
+                          stream);
+}
+

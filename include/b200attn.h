@@ -105,6 +105,30 @@ int b2a_decode_paged(const void* q, const void* k_pool, const void* v_pool,
                      void* stream);
 
 /*
+ * Paged decode that allocates nothing and takes no scratch buffer: identical
+ * arguments and results to b2a_decode_paged minus o_part/l_part.  It is for
+ * callers that cannot call cudaMalloc where they decode (an allocator-free
+ * serving runtime that reserves all device memory up front, a memory pool
+ * that must not grow, a plugin host that forbids allocation on its request
+ * path).  The split partials go to a fixed 16 MiB array inside the library
+ * that every GPU loading the library holds until exit; a call needing more
+ * than that, B*H*ceil(max_pages/pages_per_split)*(D+1) > 4,194,304 floats,
+ * is rejected with B2A_ERR_INVALID_ARG.  The first call on each device looks
+ * up that array's device address (make it before any stream capture).  All
+ * calls on one device share that device's copy of the array, which keeps the
+ * last call's contents (nothing in it has to start at zero: every entry a
+ * call reads is written earlier in the same call).  Two calls that can run
+ * at the same time on one device, e.g. on different streams, race on it and
+ * must be ordered by the caller.  No counterpart in the reference.
+ */
+int b2a_decode_paged_noalloc(const void* q, const void* k_pool,
+                             const void* v_pool, const int32_t* block_table,
+                             const int32_t* kv_lens, void* o, float* lse,
+                             int B, int H, int Hkv, int D, int page_size,
+                             int max_pages, int num_pages, int pages_per_split,
+                             int dtype, float scale, void* stream);
+
+/*
  * Device error word written by the kernels (bit 0: a bounded pipeline wait
  * timed out; bit 1: a paged-decode block-table entry was out of range).  Reads and clears the word of the current device; this
  * call synchronises the device.  *flags receives the word.
