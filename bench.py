@@ -4,7 +4,7 @@
 Default workload: BASELINE config 2, the reference's headline shape -- non-causal
 prefill forward, B=1, H=8, N=4096, D=64, fp16, returning O and L
 (bench/bench_fa3_headline.py of the reference times the same call, forward()+L).
-A step is one forward over one batch.  Other configs: --config 1|2|3|4|5a.
+A step is one forward over one batch.  Other configs: --config 1|2|3|4|4s|5a.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
 
@@ -50,6 +50,9 @@ CONFIGS = {
               shard=True, name="config3: prefill fwd B=4 H=32 N=8192 D=128 bf16 causal"),
     "4": dict(kind="decode", B=64, H=32, Hkv=8, L=16384, D=128, dtype="float16", splits=16,
               shard=True, name="config4: split-KV GQA decode B=64 H=32 Hkv=8 L=16384 D=128 fp16"),
+    # config 4 at 1/8 batch (537 MB of KV, still > L2): the case ncu section captures run on
+    "4s": dict(kind="decode", B=8, H=32, Hkv=8, L=16384, D=128, dtype="float16", splits=16,
+               shard=True, name="config4-small: split-KV GQA decode B=8 H=32 Hkv=8 L=16384 D=128 fp16"),
     "5a": dict(kind="paged", B=128, H=32, Hkv=8, D=128, page=16, lmin=512, lmax=32768,
                dtype="float16", pps=64, shard=True,
                name="config5a: paged decode B=128 H=32 Hkv=8 D=128 fp16 page=16 len U[512,32768]"),
