@@ -53,6 +53,9 @@ CONFIGS = {
     # config 4 at 1/8 batch (537 MB of KV, still > L2): the case ncu section captures run on
     "4s": dict(kind="decode", B=8, H=32, Hkv=8, L=16384, D=128, dtype="float16", splits=16,
                shard=True, name="config4-small: split-KV GQA decode B=8 H=32 Hkv=8 L=16384 D=128 fp16"),
+    "5b": dict(kind="kvshard", B=1, H=32, Hkv=8, L=131072, D=128, dtype="bfloat16", splits=64,
+               shard=True, name="config5b: KV-sharded decode B=1 H=32 Hkv=8 L=131072 D=128 bf16, "
+                                "NCCL all-gather of partials"),
     "5a": dict(kind="paged", B=128, H=32, Hkv=8, D=128, page=16, lmin=512, lmax=32768,
                dtype="float16", pps=64, shard=True,
                name="config5a: paged decode B=128 H=32 Hkv=8 D=128 fp16 page=16 len U[512,32768]"),
@@ -170,6 +173,8 @@ def cpu_sample(cfg_key: str, steps: int, warmup: int):
     # decode: one batch row per step
     if c["kind"] == "decode":
         L, D, Hkv, H = c["L"], c["D"], c["Hkv"], c["H"]
+    elif c["kind"] == "kvshard":
+        L, D, Hkv, H = c["L"] // 8, c["D"], c["Hkv"], c["H"]
     else:
         L, D, Hkv, H = int(paged_lengths(c).mean()), c["D"], c["Hkv"], c["H"]
     q = ora.seeded_normal((1, H, D), 1)
@@ -268,6 +273,39 @@ def run_ours(args, rank, world, local_rank):
 
         workload = dict(workload=c["name"], B=B, H=H, Hkv=Hkv, L=L, D=D, splits=c["splits"],
                         dtype=c["dtype"], kv_cache="resident (4.3 GB/step > L2)")
+    elif c["kind"] == "kvshard":
+        from b200attn.sharded import decode_kv_sharded
+        B, H, Hkv, D = c["B"], c["H"], c["Hkv"], c["D"]
+        assert c["L"] % world == 0
+        Ll = c["L"] // world  # this rank's contiguous slice of the sequence
+        q = torch.randn(B, H, 1, D, generator=torch.Generator().manual_seed(5)).to(tdt).to(dev)
+        k = torch.randn(B, Hkv, Ll, D, device=dev, generator=gen).to(tdt)
+        v = torch.randn(B, Hkv, Ll, D, device=dev, generator=gen).to(tdt)
+        work_per_step = 2 * B * Hkv * Ll * D * 2  # this rank's K+V bytes
+        unit = "GB/s"
+        nsets = 1
+
+        def step(i):
+            return decode_kv_sharded(q, k, v, splits=c["splits"])
+
+        kernel_regex = "decode_kernel"
+        bound = "hbm"
+        h2d = B * H * D * 2
+        d2h = B * H * D * 2 + B * H * 4
+        host_q = torch.randn(B, H, 1, D).to(tdt).pin_memory()
+        host_out = (torch.empty(B, H, 1, D, dtype=tdt).pin_memory(),
+                    torch.empty(B, H, 1, dtype=torch.float32).pin_memory())
+
+        def e2e_step(i):
+            qd = host_q.to(dev, non_blocking=True)
+            O, Lo = decode_kv_sharded(qd, k, v, splits=c["splits"])
+            host_out[0].copy_(O, non_blocking=True)
+            host_out[1].copy_(Lo, non_blocking=True)
+
+        workload = dict(workload=c["name"], B=B, H=H, Hkv=Hkv, L=c["L"], L_per_rank=Ll, D=D,
+                        splits_per_rank=c["splits"], dtype=c["dtype"],
+                        collective="all_gather_into_tensor of [B,H,S,D+1] fp32 partials"
+                                   if world > 1 else "none (1 rank)")
     else:  # paged
         lens_all = paged_lengths(c)
         # greedy balance of sequences over ranks by total length

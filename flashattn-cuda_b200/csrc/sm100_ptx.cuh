@@ -1,6 +1,6 @@
 // sm100_ptx.cuh -- thin inline-PTX wrappers for the sm_100a features the
 // attention kernels use: mbarriers with bounded waits, TMA tensor / bulk
-// copies (never with cluster multicast), and tcgen05 (UMMA + TMEM).
+// copies (plain per-CTA loads only), and tcgen05 (UMMA + TMEM).
 //
 // Encodings of the UMMA shared-memory and instruction descriptors follow the
 // PTX ISA description of tcgen05 matrix descriptors (64-bit shared-memory
@@ -91,7 +91,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tensor and bulk).  No .multicast::cluster anywhere in this library.
+// TMA (tensor and bulk).  Every load here is a plain per-CTA copy (no cluster
+// broadcast of any kind).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
