@@ -506,6 +506,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    # Libraries (NCCL's version banner at communicator set-up) may write to fd 1;
+    # keep stdout for the one JSON line by sending everything else to stderr.
+    json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
 
     if args.impl == "reference":
         out = run_reference(args, rank, world)
@@ -520,7 +524,9 @@ def main():
             import torch.distributed as dist
             dist.destroy_process_group()
     if out is not None:
-        print(json.dumps(out), flush=True)
+        sys.stdout.flush()
+        json_out.write(json.dumps(out) + "\n")
+        json_out.flush()
 
 
 if __name__ == "__main__":

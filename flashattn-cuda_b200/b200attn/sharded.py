@@ -32,13 +32,20 @@ class ShardMismatchError(RuntimeError):
     """Ranks disagree on the partial shapes (batch, heads, splits or head dim)."""
 
 
+# (group, shape) pairs whose agreement across ranks has been checked.  The check
+# costs a collective and a host synchronisation, so it runs once per shape, not
+# once per decode step.
+_checked_shapes: set = set()
+
+
 def gather_partials(o_part: torch.Tensor, l_part: torch.Tensor, group=None,
                     check_shapes: bool = True):
     """All-gather per-rank partials; returns (o_all [B,H,world*S,D], l_all [B,H,world*S])
     with rank r's splits at positions [r*S, (r+1)*S) (sequence order)."""
     world = dist.get_world_size(group)
     B, H, S, D = o_part.shape
-    if check_shapes:
+    key = (id(group), world, B, H, S, D)
+    if check_shapes and key not in _checked_shapes:
         shape = torch.tensor([B, H, S, D], dtype=torch.int64, device=o_part.device)
         shapes = [torch.empty_like(shape) for _ in range(world)]
         dist.all_gather(shapes, shape, group=group)
@@ -47,6 +54,7 @@ def gather_partials(o_part: torch.Tensor, l_part: torch.Tensor, group=None,
                 raise ShardMismatchError(
                     f"rank {r} partials have shape {tuple(s.tolist())}, this rank "
                     f"{tuple(shape.tolist())}: every rank must use the same B, H, splits, D")
+        _checked_shapes.add(key)
     packed = torch.cat([o_part.float(), l_part.float().unsqueeze(-1)], dim=-1).contiguous()
     out = torch.empty((world * B, H, S, D + 1), dtype=packed.dtype, device=packed.device)
     dist.all_gather_into_tensor(out, packed, group=group)  # rank blocks along dim 0
