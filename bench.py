@@ -257,6 +257,13 @@ def run_ours(args, rank, world, local_rank):
         def step(i):
             return b200attn.decode(q, k, v, splits=c["splits"])
 
+        if args.graph:
+            from b200attn.graphs import CapturedDecode
+            cap = CapturedDecode(q, k, v, splits=c["splits"])
+
+            def step(i):  # noqa: F811
+                return cap()
+
         kernel_regex = "decode_kernel"
         bound = "hbm"
         h2d = B * H * D * 2
@@ -267,7 +274,7 @@ def run_ours(args, rank, world, local_rank):
 
         def e2e_step(i):
             qd = host_q.to(dev, non_blocking=True)
-            O, Lo = b200attn.decode(qd, k, v, splits=c["splits"])
+            O, Lo = cap(qd) if args.graph else b200attn.decode(qd, k, v, splits=c["splits"])
             host_out[0].copy_(O, non_blocking=True)
             host_out[1].copy_(Lo, non_blocking=True)
 
@@ -288,6 +295,13 @@ def run_ours(args, rank, world, local_rank):
         def step(i):
             return decode_kv_sharded(q, k, v, splits=c["splits"])
 
+        if args.graph:
+            from b200attn.graphs import CapturedDecode
+            cap = CapturedDecode(q, k, v, splits=c["splits"], sharded=True)
+
+            def step(i):  # noqa: F811
+                return cap()
+
         kernel_regex = "decode_kernel"
         bound = "hbm"
         h2d = B * H * D * 2
@@ -298,14 +312,15 @@ def run_ours(args, rank, world, local_rank):
 
         def e2e_step(i):
             qd = host_q.to(dev, non_blocking=True)
-            O, Lo = decode_kv_sharded(qd, k, v, splits=c["splits"])
+            O, Lo = cap(qd) if args.graph else decode_kv_sharded(qd, k, v, splits=c["splits"])
             host_out[0].copy_(O, non_blocking=True)
             host_out[1].copy_(Lo, non_blocking=True)
 
         workload = dict(workload=c["name"], B=B, H=H, Hkv=Hkv, L=c["L"], L_per_rank=Ll, D=D,
                         splits_per_rank=c["splits"], dtype=c["dtype"],
                         collective="all_gather_into_tensor of [B,H,S,D+1] fp32 partials"
-                                   if world > 1 else "none (1 rank)")
+                                   if world > 1 else "none (1 rank)",
+                        cuda_graph=bool(args.graph))
     else:  # paged
         lens_all = paged_lengths(c)
         # greedy balance of sequences over ranks by total length
@@ -373,19 +388,24 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    # per-launch events for the dominant kernel (same stream)
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
     ev0.record(stream)
     for i in range(args.steps):
-        kev[i][0].record(stream)
         step(args.warmup + i)
-        kev[i][1].record(stream)
     ev1.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
     clocks = sampler.stop()
     ms = ev0.elapsed_time(ev1)
+
+    # ---- per-step device time of the dominant kernel(s), for the roofline: a
+    # separate pass, because events between steps add a few microseconds each
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for i in range(args.steps):
+        kev[i][0].record(stream)
+        step(args.warmup + i)
+        kev[i][1].record(stream)
+    torch.cuda.synchronize(dev)
     step_ms = [a.elapsed_time(b) for a, b in kev]
 
     # ---- end-to-end through the public API with host buffers
@@ -436,7 +456,7 @@ def run_ours(args, rank, world, local_rank):
             v, u, sample, cores = cpu_sample(args.config, steps=2, warmup=1)
             cpu = {"value": round(v, 6), "unit": u, "cores": cores, "kind": "port",
                    "sample": sample}
-        kernel_launches = args.steps * (1 if c["kind"] == "prefill" else 2)
+        kernel_launches = args.steps * (1 if c["kind"] == "prefill" else 2)  # timed region only
         out = {
             "metric": METRIC,
             "value": round(value, 3),
@@ -500,6 +520,8 @@ def main():
     ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="decode configs: replay each step as one captured CUDA graph")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
