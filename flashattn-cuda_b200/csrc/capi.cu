@@ -270,6 +270,7 @@ int b2a_device_error(uint32_t* flags) {
     return set_error(B2A_ERR_NO_DEVICE, "b200attn requires a current sm_100 (B200) CUDA device");
   uint32_t v = 0;
   B2A_TRY(take_error_flags_prefill(&v));
+  B2A_TRY(take_error_flags_prefill_d64(&v));
   B2A_TRY(take_error_flags_decode(&v));
   *flags = v;
   return B2A_OK;

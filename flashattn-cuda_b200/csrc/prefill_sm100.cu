@@ -394,13 +394,11 @@ int prefill_dispatch(const void* q, const void* k, const void* v, void* o, float
                      int Hkv, int N, int D, int dtype, int causal, float scale,
                      cudaStream_t stream) {
   const bool bf = dtype == B2A_BF16;
+  // D = 64: the split-row kernel of prefill_d64_sm100.cu
+  if (D == 64) return prefill_d64_dispatch(q, k, v, o, lse, B, H, Hkv, N, dtype, causal, scale, stream);
 #define B2A_PF(DD, BB, CC) \
   if (D == DD && bf == BB && (causal != 0) == CC) \
     return launch_prefill<DD, BB, CC>(q, k, v, o, lse, B, H, Hkv, N, scale, stream);
-  B2A_PF(64, false, false)
-  B2A_PF(64, false, true)
-  B2A_PF(64, true, false)
-  B2A_PF(64, true, true)
   B2A_PF(128, false, false)
   B2A_PF(128, false, true)
   B2A_PF(128, true, false)
