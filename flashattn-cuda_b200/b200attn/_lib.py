@@ -23,6 +23,9 @@ _SIGNATURES = {
     # q k v o lse | B H Hkv N D | dtype causal scale stream
     "b2a_prefill_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp] + [_c_int] * 5
                         + [_c_int, _c_int, _c_float, _vp]),
+    # q k v o lse | B H Hkv N Nk D | dtype causal scale stream
+    "b2a_prefill_fwd_kv": (_c_int, [_vp, _vp, _vp, _vp, _vp] + [_c_int] * 6
+                           + [_c_int, _c_int, _c_float, _vp]),
     # q k v o_part l_part | B H Hkv Lkv D splits | dtype scale stream
     "b2a_decode_splitkv": (_c_int, [_vp] * 5 + [_c_int] * 6 + [_c_int, _c_float, _vp]),
     # o_part l_part o lse | B H splits D dtype | stream
@@ -31,6 +34,8 @@ _SIGNATURES = {
     "b2a_decode_paged": (_c_int, [_vp] * 9 + [_c_int] * 8 + [_c_int, _c_float, _vp]),
     # q kp vp bt lens o lse | B H Hkv D page max_pages num_pages pps | dtype scale stream
     "b2a_decode_paged_noalloc": (_c_int, [_vp] * 7 + [_c_int] * 8 + [_c_int, _c_float, _vp]),
+    # k_new v_new k_pool v_pool bt lens | B Hkv T D page max_pages num_pages dtype advance | stream
+    "b2a_kv_append_paged": (_c_int, [_vp] * 6 + [_c_int] * 9 + [_vp]),
     "b2a_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint32)]),
 }
 

@@ -11,7 +11,9 @@ under a device guard (:365, :380).
 
 Additions over the reference, all opt-in: bf16 inputs compute and return bf16
 (the reference would cast them to fp16), D = 128, `causal=True`, an explicit
-`scale`, GQA (K/V with fewer heads than Q), and the decode entry points
+`scale`, GQA (K/V with fewer heads than Q), a key length Nk different from
+the query length N (causal masks aligned to the last key), and the decode
+entry points
 `decode_splitkv`, `decode_combine`, `decode` and `decode_paged`.
 """
 from __future__ import annotations
@@ -48,10 +50,13 @@ def _prefill(Q, K, V, want_L: bool, causal: bool, scale: Optional[float]):
         raise RuntimeError("Head dimension must be 64 or 128")
     if N <= 0:
         raise RuntimeError("N must be > 0")
-    if (K.dim() != 4 or K.shape != V.shape or K.shape[0] != B or K.shape[2] != N
-            or K.shape[3] != D or K.shape[1] <= 0 or H % K.shape[1] != 0):
-        raise RuntimeError("K and V must have the same shape as Q (self-attention only)"
-                           " up to a KV head count that divides H")
+    if (K.dim() != 4 or K.shape != V.shape or K.shape[0] != B or K.shape[3] != D
+            or K.shape[1] <= 0 or H % K.shape[1] != 0 or K.shape[2] <= 0):
+        raise RuntimeError("K and V must have the same shape as Q (self-attention) up to a KV"
+                           " head count that divides H and a key length Nk")
+    Nk = K.shape[2]
+    if causal and Nk < N:
+        raise RuntimeError("causal attention needs Nk >= N (the mask is aligned to the last key)")
     if K.device != Q.device or V.device != Q.device:
         raise RuntimeError("Q/K/V must be on the same device")
     Hkv = K.shape[1]
@@ -64,9 +69,9 @@ def _prefill(Q, K, V, want_L: bool, causal: bool, scale: Optional[float]):
         O = torch.empty((B, H, N, D), dtype=dt, device=Q.device)
         L = torch.empty((B, H, N), dtype=torch.float32, device=Q.device) if want_L else None
         s = float(D) ** -0.5 if scale is None else float(scale)
-        _lib.check(lib.b2a_prefill_fwd(
+        _lib.check(lib.b2a_prefill_fwd_kv(
             Qc.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), O.data_ptr(), _ptr(L),
-            B, H, Hkv, N, D, _DT[dt], int(bool(causal)), s, _stream(Q.device)))
+            B, H, Hkv, N, Nk, D, _DT[dt], int(bool(causal)), s, _stream(Q.device)))
     return O, L
 
 

@@ -29,6 +29,7 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uin
 // Read-and-clear of each translation unit's device error word.
 int take_error_flags_prefill(uint32_t* flags);
 int take_error_flags_prefill_d64(uint32_t* flags);
+int take_error_flags_kvcache(uint32_t* flags);
 int take_error_flags_decode(uint32_t* flags);
 
 // Defines take_error_flags_<unit>() for the unit that expands it.
@@ -45,15 +46,19 @@ int take_error_flags_decode(uint32_t* flags);
 
 // Kernel dispatchers (defined next to their kernels).
 int prefill_dispatch(const void* q, const void* k, const void* v, void* o, float* lse, int B,
-                     int H, int Hkv, int N, int D, int dtype, int causal, float scale,
+                     int H, int Hkv, int N, int Nk, int D, int dtype, int causal, float scale,
                      cudaStream_t stream);
 int prefill_d64_dispatch(const void* q, const void* k, const void* v, void* o, float* lse, int B,
-                         int H, int Hkv, int N, int dtype, int causal, float scale,
+                         int H, int Hkv, int N, int Nk, int dtype, int causal, float scale,
                          cudaStream_t stream);
 int decode_dispatch(const void* q, const void* k, const void* v, const int32_t* block_table,
                     const int32_t* kv_lens, float* o_part, float* l_part, int B, int H, int Hkv,
                     int Lkv, int D, int splits, int tokens_per_split, int page_size, int max_pages,
                     int num_pages, int dtype, float scale, cudaStream_t stream);
+int kv_append_dispatch(const void* k_new, const void* v_new, void* k_pool, void* v_pool,
+                       const int32_t* block_table, int32_t* kv_lens, int B, int Hkv, int T, int D,
+                       int page_size, int max_pages, int num_pages, int advance,
+                       cudaStream_t stream);
 int combine_dispatch(const float* o_part, const float* l_part, void* o, float* lse, int B, int H,
                      int splits, int D, int dtype, const int32_t* kv_lens, int tokens_per_split,
                      cudaStream_t stream);

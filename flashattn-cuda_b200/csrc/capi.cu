@@ -161,12 +161,16 @@ const char* b2a_last_error(void) { return t_last_error; }
 
 const char* b2a_version(void) { return "0.1.0"; }
 
-int b2a_prefill_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H,
-                    int Hkv, int N, int D, int dtype, int causal, float scale, void* stream) {
+int b2a_prefill_fwd_kv(const void* q, const void* k, const void* v, void* o, float* lse, int B,
+                       int H, int Hkv, int N, int Nk, int D, int dtype, int causal, float scale,
+                       void* stream) {
   t_last_error[0] = 0;
   B2A_TRY(common_checks(dtype));
   if (D != 64 && D != 128) return set_error(B2A_ERR_UNSUPPORTED, "Head dimension must be 64 or 128");
-  if (N <= 0) return set_error(B2A_ERR_INVALID_ARG, "N must be > 0");
+  if (N <= 0 || Nk <= 0) return set_error(B2A_ERR_INVALID_ARG, "N must be > 0");
+  if (causal && Nk < N)
+    return set_error(B2A_ERR_INVALID_ARG,
+                     "causal attention needs Nk >= N (the mask is aligned to the last key)");
   if (B <= 0 || H <= 0 || Hkv <= 0) return set_error(B2A_ERR_INVALID_ARG, "B, H and Hkv must be > 0");
   if (H % Hkv != 0) return set_error(B2A_ERR_INVALID_ARG, "H must be a multiple of Hkv");
   if ((int64_t)B * H > 0x7fffffff) return set_error(B2A_ERR_INVALID_ARG, "B*H too large");
@@ -177,8 +181,13 @@ int b2a_prefill_fwd(const void* q, const void* k, const void* v, void* o, float*
   B2A_TRY(check_device_ptr(v, "V"));
   B2A_TRY(check_device_ptr(o, "O"));
   if (lse != nullptr) B2A_TRY(check_device_ptr(lse, "L"));
-  return prefill_dispatch(q, k, v, o, lse, B, H, Hkv, N, D, dtype, causal, scale,
+  return prefill_dispatch(q, k, v, o, lse, B, H, Hkv, N, Nk, D, dtype, causal, scale,
                           static_cast<cudaStream_t>(stream));
+}
+
+int b2a_prefill_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H,
+                    int Hkv, int N, int D, int dtype, int causal, float scale, void* stream) {
+  return b2a_prefill_fwd_kv(q, k, v, o, lse, B, H, Hkv, N, N, D, dtype, causal, scale, stream);
 }
 
 int b2a_decode_splitkv(const void* q, const void* k, const void* v, float* o_part, float* l_part,
@@ -263,6 +272,28 @@ int b2a_decode_paged(const void* q, const void* k_pool, const void* v_pool,
   return combine_dispatch(o_part, l_part, o, lse, B, H, splits, D, dtype, kv_lens, tps, s);
 }
 
+int b2a_kv_append_paged(const void* k_new, const void* v_new, void* k_pool, void* v_pool,
+                        const int32_t* block_table, int32_t* kv_lens, int B, int Hkv, int T,
+                        int D, int page_size, int max_pages, int num_pages, int dtype,
+                        int advance_lens, void* stream) {
+  t_last_error[0] = 0;
+  B2A_TRY(common_checks(dtype));
+  if (D != 64 && D != 128) return set_error(B2A_ERR_UNSUPPORTED, "Head dimension must be 64 or 128");
+  if (B <= 0 || Hkv <= 0 || T <= 0 || page_size <= 0 || max_pages <= 0 || num_pages <= 0)
+    return set_error(B2A_ERR_INVALID_ARG,
+                     "B, Hkv, T, page_size, max_pages and num_pages must be > 0");
+  if (B > 65535 || Hkv > 65535) return set_error(B2A_ERR_INVALID_ARG, "B and Hkv must be <= 65535");
+  B2A_TRY(check_device_ptr(k_new, "k_new"));
+  B2A_TRY(check_device_ptr(v_new, "v_new"));
+  B2A_TRY(check_device_ptr(k_pool, "k_pool"));
+  B2A_TRY(check_device_ptr(v_pool, "v_pool"));
+  B2A_TRY(check_device_ptr(block_table, "block_table"));
+  B2A_TRY(check_device_ptr(kv_lens, "kv_lens"));
+  return kv_append_dispatch(k_new, v_new, k_pool, v_pool, block_table, kv_lens, B, Hkv, T, D,
+                            page_size, max_pages, num_pages, advance_lens,
+                            static_cast<cudaStream_t>(stream));
+}
+
 int b2a_device_error(uint32_t* flags) {
   t_last_error[0] = 0;
   if (flags == nullptr) return set_error(B2A_ERR_INVALID_ARG, "flags must not be null");
@@ -271,6 +302,7 @@ int b2a_device_error(uint32_t* flags) {
   uint32_t v = 0;
   B2A_TRY(take_error_flags_prefill(&v));
   B2A_TRY(take_error_flags_prefill_d64(&v));
+  B2A_TRY(take_error_flags_kvcache(&v));
   B2A_TRY(take_error_flags_decode(&v));
   *flags = v;
   return B2A_OK;

@@ -66,7 +66,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefill_d64_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, void* __restrict__ out,
-                       float* __restrict__ lse, int N, int H, int group, float scale_log2) {
+                       float* __restrict__ lse, int N, int Nk, int H, int group, float scale_log2) {
   using E = Elem<BF16>;
   constexpr int S = kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -92,11 +92,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int bh = blockIdx.x;
   const int bhk = (bh / H) * (H / group) + (bh % H) / group;
   const int q0 = ((int)gridDim.y - 1 - (int)blockIdx.y) * kRowsPerCta;
-  const int nkv_all = (N + BN - 1) / BN;
+  // keys: Nk (>= N when causal); the causal mask is aligned to the bottom
+  // right, query row r sees keys <= r + (Nk - N)
+  const int koff = Nk - N;
+  const int nkv_all = (Nk + BN - 1) / BN;
   int nkv_t[2];
 #pragma unroll
   for (int t = 0; t < 2; ++t)
-    nkv_t[t] = CAUSAL ? min(nkv_all, (q0 + (t + 1) * BM + BN - 1) / BN) : nkv_all;
+    nkv_t[t] = CAUSAL ? min(nkv_all, (q0 + (t + 1) * BM + koff + BN - 1) / BN) : nkv_all;
   const int nkv = nkv_t[1];
 
   if (warp == kProducerWarp && lane == 0) {
@@ -222,9 +225,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_wait();
 
       const int kv0 = j * BN + h * HALF;
-      const bool need_mask = (kv0 + HALF > N) || (CAUSAL && kv0 + HALF > q0 + t * BM);
+      const bool need_mask = (kv0 + HALF > Nk) || (CAUSAL && kv0 + HALF > q0 + t * BM + koff);
       if (need_mask) {
-        const int lim = (CAUSAL ? min(N, grow + 1) : N) - kv0;
+        const int lim = (CAUSAL ? min(Nk, grow + 1 + koff) : Nk) - kv0;
 #pragma unroll
         for (int c = 0; c < HALF; ++c)
           if (c >= lim) s[c] = -INFINITY;
@@ -346,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <bool BF16, bool CAUSAL>
 static int launch_prefill_d64(const void* q, const void* k, const void* v, void* o, float* lse,
-                              int B, int H, int Hkv, int N, float scale, cudaStream_t stream) {
+                              int B, int H, int Hkv, int N, int Nk, float scale, cudaStream_t stream) {
   using namespace prefill64;
   auto kern = prefill_d64_kernel<BF16, CAUSAL>;
   static bool attr_done[kMaxDevices] = {};
@@ -363,11 +366,11 @@ static int launch_prefill_d64(const void* q, const void* k, const void* v, void*
   const CUtensorMapDataType dt =
       BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   int rc = make_tmap_3d(&tq, q, dt, D, N, (uint64_t)B * H, 64, BM, true);
-  if (rc == B2A_OK) rc = make_tmap_3d(&tk, k, dt, D, N, (uint64_t)B * Hkv, 64, BN, true);
-  if (rc == B2A_OK) rc = make_tmap_3d(&tv, v, dt, D, N, (uint64_t)B * Hkv, 64, BN, true);
+  if (rc == B2A_OK) rc = make_tmap_3d(&tk, k, dt, D, Nk, (uint64_t)B * Hkv, 64, BN, true);
+  if (rc == B2A_OK) rc = make_tmap_3d(&tv, v, dt, D, Nk, (uint64_t)B * Hkv, 64, BN, true);
   if (rc != B2A_OK) return rc;
   dim3 grid((unsigned)(B * H), (unsigned)((N + kRowsPerCta - 1) / kRowsPerCta));
-  kern<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, o, lse, N, H, H / Hkv,
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, o, lse, N, Nk, H, H / Hkv,
                                                scale * 1.4426950408889634f);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "prefill d64 kernel launch");
@@ -375,15 +378,15 @@ static int launch_prefill_d64(const void* q, const void* k, const void* v, void*
 }
 
 int prefill_d64_dispatch(const void* q, const void* k, const void* v, void* o, float* lse, int B,
-                         int H, int Hkv, int N, int dtype, int causal, float scale,
+                         int H, int Hkv, int N, int Nk, int dtype, int causal, float scale,
                          cudaStream_t stream) {
   const bool bf = dtype == B2A_BF16;
   if (bf) {
-    return causal ? launch_prefill_d64<true, true>(q, k, v, o, lse, B, H, Hkv, N, scale, stream)
-                  : launch_prefill_d64<true, false>(q, k, v, o, lse, B, H, Hkv, N, scale, stream);
+    return causal ? launch_prefill_d64<true, true>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, stream)
+                  : launch_prefill_d64<true, false>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, stream);
   }
-  return causal ? launch_prefill_d64<false, true>(q, k, v, o, lse, B, H, Hkv, N, scale, stream)
-                : launch_prefill_d64<false, false>(q, k, v, o, lse, B, H, Hkv, N, scale, stream);
+  return causal ? launch_prefill_d64<false, true>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, stream)
+                : launch_prefill_d64<false, false>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, stream);
 }
 
 B2A_DEFINE_ERROR_READER(prefill_d64)

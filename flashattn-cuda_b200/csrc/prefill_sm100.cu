@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, void* __restrict__ out,
-                       float* __restrict__ lse, int N, int H, int group, float scale_log2) {
+                       float* __restrict__ lse, int N, int Nk, int H, int group, float scale_log2) {
   using C = Cfg<D>;
   using E = Elem<BF16>;
   constexpr int S = C::kStages;
@@ -106,12 +106,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int bhk = (bh / H) * (H / group) + (bh % H) / group;  // KV head of this query head
   const int qb = (int)gridDim.y - 1 - (int)blockIdx.y;
   const int q0 = qb * kRowsPerCta;
-  const int nkv_all = (N + BN - 1) / BN;
+  // keys: Nk (>= N when causal); the causal mask is aligned to the bottom
+  // right, query row r sees keys <= r + (Nk - N)
+  const int koff = Nk - N;
+  const int nkv_all = (Nk + BN - 1) / BN;
   // KV tiles Q tile t needs (t = 0, 1); the loop runs to the larger one
   int nkv_t[kQTiles];
 #pragma unroll
   for (int t = 0; t < kQTiles; ++t)
-    nkv_t[t] = CAUSAL ? min(nkv_all, (q0 + (t + 1) * BM + BN - 1) / BN) : nkv_all;
+    nkv_t[t] = CAUSAL ? min(nkv_all, (q0 + (t + 1) * BM + koff + BN - 1) / BN) : nkv_all;
   const int nkv = nkv_t[kQTiles - 1];
 
   if (warp == kProducerWarp && lane == 0) {
@@ -246,9 +249,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_wait();
 
       const int kv0 = j * BN;
-      const bool need_mask = (kv0 + BN > N) || (CAUSAL && kv0 + BN > q0 + t * BM);
+      const bool need_mask = (kv0 + BN > Nk) || (CAUSAL && kv0 + BN > q0 + t * BM + koff);
       if (need_mask) {
-        const int lim = (CAUSAL ? min(N, grow + 1) : N) - kv0;  // first masked column
+        const int lim = (CAUSAL ? min(Nk, grow + 1 + koff) : Nk) - kv0;  // first masked column
 #pragma unroll
         for (int c = 0; c < BN; ++c)
           if (c >= lim) s[c] = -INFINITY;
@@ -358,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 template <int D, bool BF16, bool CAUSAL>
 static int launch_prefill(const void* q, const void* k, const void* v, void* o, float* lse, int B,
-                          int H, int Hkv, int N, float scale, cudaStream_t stream) {
+                          int H, int Hkv, int N, int Nk, float scale, cudaStream_t stream) {
   using namespace prefill;
   using C = Cfg<D>;
   auto kern = prefill_fwd_kernel<D, BF16, CAUSAL>;
@@ -376,13 +379,13 @@ static int launch_prefill(const void* q, const void* k, const void* v, void* o, 
   const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   int rc = make_tmap_3d(&tq, q, dt, D, N, (uint64_t)B * H, 64, BM, /*swizzle128=*/true);
   if (rc != B2A_OK) return rc;
-  rc = make_tmap_3d(&tk, k, dt, D, N, (uint64_t)B * Hkv, 64, BN, true);
+  rc = make_tmap_3d(&tk, k, dt, D, Nk, (uint64_t)B * Hkv, 64, BN, true);
   if (rc != B2A_OK) return rc;
-  rc = make_tmap_3d(&tv, v, dt, D, N, (uint64_t)B * Hkv, 64, BN, true);
+  rc = make_tmap_3d(&tv, v, dt, D, Nk, (uint64_t)B * Hkv, 64, BN, true);
   if (rc != B2A_OK) return rc;
   dim3 grid((unsigned)(B * H), (unsigned)((N + kRowsPerCta - 1) / kRowsPerCta));
   const float scale_log2 = scale * 1.4426950408889634f;
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, o, lse, N, H, H / Hkv, scale_log2);
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, o, lse, N, Nk, H, H / Hkv, scale_log2);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "prefill kernel launch");
   return B2A_OK;
@@ -391,14 +394,14 @@ static int launch_prefill(const void* q, const void* k, const void* v, void* o, 
 B2A_DEFINE_ERROR_READER(prefill)
 
 int prefill_dispatch(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H,
-                     int Hkv, int N, int D, int dtype, int causal, float scale,
+                     int Hkv, int N, int Nk, int D, int dtype, int causal, float scale,
                      cudaStream_t stream) {
   const bool bf = dtype == B2A_BF16;
   // D = 64: the split-row kernel of prefill_d64_sm100.cu
-  if (D == 64) return prefill_d64_dispatch(q, k, v, o, lse, B, H, Hkv, N, dtype, causal, scale, stream);
+  if (D == 64) return prefill_d64_dispatch(q, k, v, o, lse, B, H, Hkv, N, Nk, dtype, causal, scale, stream);
 #define B2A_PF(DD, BB, CC) \
   if (D == DD && bf == BB && (causal != 0) == CC) \
-    return launch_prefill<DD, BB, CC>(q, k, v, o, lse, B, H, Hkv, N, scale, stream);
+    return launch_prefill<DD, BB, CC>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, stream);
   B2A_PF(128, false, false)
   B2A_PF(128, false, true)
   B2A_PF(128, true, false)

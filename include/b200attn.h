@@ -63,6 +63,19 @@ int b2a_prefill_fwd(const void* q, const void* k, const void* v, void* o,
                     int dtype, int causal, float scale, void* stream);
 
 /*
+ * Prefill forward with a key/value length Nk that may differ from the query
+ * length N (cross-attention, or a chunk of N new queries over a cache of Nk
+ * keys): Q,O [B,H,N,D], K,V [B,Hkv,Nk,D], lse [B,H,N].  With causal != 0 the
+ * mask is aligned to the last key -- query row r sees keys 0 .. r + Nk - N --
+ * and Nk >= N is required.  b2a_prefill_fwd is the Nk == N case.  The
+ * reference requires K and V to have Q's shape
+ * (cuda/flash_attn_fa3_db_full.cu:358-359); this lifts that restriction.
+ */
+int b2a_prefill_fwd_kv(const void* q, const void* k, const void* v, void* o,
+                       float* lse, int B, int H, int Hkv, int N, int Nk, int D,
+                       int dtype, int causal, float scale, void* stream);
+
+/*
  * Split-KV decode, first stage: for each (batch, query head, split) the
  * softmax-normalised partial output and its natural-log sum of exp.  The KV
  * sequence of length Lkv is cut into `splits` chunks of ceil(Lkv/splits)
@@ -105,6 +118,22 @@ int b2a_decode_paged(const void* q, const void* k_pool, const void* v_pool,
                      void* stream);
 
 /*
+ * Append T new tokens per sequence to a paged KV cache (the write path of
+ * b2a_decode_paged): k_new, v_new [B,Hkv,T,D] go to positions kv_lens[b] + t
+ * of sequence b, i.e. page block_table[b, pos / page_size], slot pos %
+ * page_size of k_pool / v_pool [P,Hkv,page_size,D].  The block table must
+ * already hold a page for every written position (a missing or out-of-range
+ * entry sets bit 2 of the device error word and that token is not written).
+ * With advance_lens != 0, kv_lens[b] += T afterwards (same stream).  No
+ * counterpart in the reference.
+ */
+int b2a_kv_append_paged(const void* k_new, const void* v_new, void* k_pool,
+                        void* v_pool, const int32_t* block_table,
+                        int32_t* kv_lens, int B, int Hkv, int T, int D,
+                        int page_size, int max_pages, int num_pages, int dtype,
+                        int advance_lens, void* stream);
+
+/*
  * Paged decode that allocates nothing and takes no scratch buffer: identical
  * arguments and results to b2a_decode_paged minus o_part/l_part.  It is for
  * callers that cannot call cudaMalloc where they decode (an allocator-free
@@ -130,8 +159,10 @@ int b2a_decode_paged_noalloc(const void* q, const void* k_pool,
 
 /*
  * Device error word written by the kernels (bit 0: a bounded pipeline wait
- * timed out; bit 1: a paged-decode block-table entry was out of range).  Reads and clears the word of the current device; this
- * call synchronises the device.  *flags receives the word.
+ * timed out; bit 1: a paged-decode block-table entry was out of range;
+ * bit 2: a KV append found no page for a position).  Reads and clears the
+ * word of the current device; this call synchronises the device.  *flags
+ * receives the word.
  */
 int b2a_device_error(uint32_t* flags);
 

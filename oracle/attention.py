@@ -54,7 +54,10 @@ def attention_head(q, k, v, scale, causal=False, row_offset=0, dtype=np.float64)
 
 
 def naive_attention(Q, K, V, scale=None, causal=False, dtype=np.float64):
-    """Q [B,H,N,D], K/V [B,Hkv,N,D] -> (O [B,H,N,D], L [B,H,N]) (ref/naive_attn.py:10-38)."""
+    """Q [B,H,N,D], K/V [B,Hkv,Nk,D] -> (O [B,H,N,D], L [B,H,N]) (ref/naive_attn.py:10-38).
+
+    With Nk != N the causal mask is aligned to the last key: row r sees keys
+    0 .. r + Nk - N (the reference only has Nk == N)."""
     Q = np.asarray(Q)
     B, H, N, D = Q.shape
     Hkv = K.shape[1]
@@ -65,7 +68,7 @@ def naive_attention(Q, K, V, scale=None, causal=False, dtype=np.float64):
         for h in range(H):
             hk = _kv_head(h, H, Hkv)
             O[b, h], L[b, h] = attention_head(Q[b, h], K[b, hk], V[b, hk], scale, causal,
-                                              0, dtype)
+                                              K.shape[2] - N, dtype)
     return O, L
 
 

@@ -105,3 +105,13 @@ def test_paged_gather_equals_contiguous():
         assert kc.shape == (Hkv, lens[b], D)
         o, l = ora.decode(q[b:b + 1], kc[None], ora.paged_gather(vp, bt[b], lens[b])[None])
         np.testing.assert_allclose(O[b], o[0], rtol=1e-12, atol=1e-12)
+
+
+def test_causal_cross_mask_aligned_to_last_key():
+    q = ora.seeded_normal((1, 1, 5, 16), 20)
+    k = ora.seeded_normal((1, 1, 9, 16), 21)
+    v = ora.seeded_normal((1, 1, 9, 16), 22)
+    O, L = ora.naive_attention(q, k, v, causal=True)
+    for r in range(5):  # row r sees keys 0 .. r + 4
+        o, l = ora.attention_head(q[0, 0, r:r + 1], k[0, 0, :r + 5], v[0, 0, :r + 5], 0.25)
+        np.testing.assert_allclose(O[0, 0, r], o[0], rtol=1e-12, atol=1e-12)

@@ -156,3 +156,32 @@ def test_no_device_errors_recorded(b2a):
     b2a.forward(q, k, v, causal=True)
     torch.cuda.synchronize()
     assert b2a.device_error_flags() == 0
+
+
+CROSS = [
+    # B, H, Hkv, N, Nk, D, dtype, causal
+    (1, 4, 4, 256, 1000, 64, torch.float16, False),
+    (1, 4, 2, 129, 700, 128, torch.bfloat16, True),    # a chunk of queries over a longer cache
+    (2, 2, 2, 300, 77, 64, torch.float16, False),      # fewer keys than queries
+    (1, 8, 8, 64, 4096, 64, torch.float16, True),
+    (1, 2, 2, 1, 513, 128, torch.float16, True),       # one query row over a cache
+]
+
+
+@pytest.mark.parametrize("B,H,Hkv,N,Nk,D,dt,causal", CROSS, ids=lambda x: str(x))
+def test_cross_attention_nq_ne_nk(b2a, B, H, Hkv, N, Nk, D, dt, causal):
+    q, _, _ = seeded((B, H, N, D), (B, Hkv, N, D), 300 + N, 1.0, dt)
+    k = dev(ora.seeded_normal((B, Hkv, Nk, D), 400 + Nk), dt)
+    v = dev(ora.seeded_normal((B, Hkv, Nk, D), 500 + Nk), dt)
+    O, L = b2a.forward(q, k, v, causal=causal)
+    Or, Lr = ora.naive_attention(host(q), host(k), host(v), causal=causal)
+    name = "bfloat16" if dt == torch.bfloat16 else "float16"
+    assert_parity(O, L, Or, Lr, name, 1.0, f"N={N} Nk={Nk}")
+    assert torch.equal(b2a.forward_only(q, k, v, causal=causal), O)
+
+
+def test_causal_needs_nk_at_least_n(b2a):
+    q = torch.zeros(1, 1, 128, 64, dtype=torch.float16, device="cuda")
+    k = torch.zeros(1, 1, 64, 64, dtype=torch.float16, device="cuda")
+    with pytest.raises(RuntimeError, match="Nk >= N"):
+        b2a.forward(q, k, k, causal=True)
