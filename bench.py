@@ -76,7 +76,8 @@ def paged_lengths(c):
 
 # ---------------------------------------------------------------- clock probe
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms while the GPU runs the
+    workload: from the warm-up, across the timed region, to one sample after it."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -93,10 +94,18 @@ class ClockSampler:
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+
+    def count(self) -> int:
+        """Samples written so far."""
+        try:
+            with open(self.path) as f:
+                return sum(1 for line in f if line.strip())
+        except Exception:
+            return 0
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -375,15 +384,21 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
-    # ---- warm-up
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize(dev)
-
-    # ---- timed device-resident region
+    # ---- warm-up, started after the clock sampler so that the GPU is not left
+    # idle between the warm-up and the timed region
     sampler = ClockSampler(local_rank)
     sampler.start()
-    time.sleep(0.3)
+    for i in range(args.warmup):
+        step(i)
+    # keep the GPU busy until the sampler is producing samples (at most ~3 s)
+    t_end = time.time() + 3.0
+    n0 = sampler.count()
+    while sampler.proc is not None and sampler.count() < n0 + 2 and time.time() < t_end:
+        for i in range(4):
+            step(i)
+        torch.cuda.synchronize(dev)
+
+    # ---- timed device-resident region (barrier + synchronize on both sides)
     barrier()
     torch.cuda.synchronize(dev)
     ev0 = torch.cuda.Event(enable_timing=True)
@@ -394,8 +409,15 @@ def run_ours(args, rank, world, local_rank):
     ev1.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
-    clocks = sampler.stop()
     ms = ev0.elapsed_time(ev1)
+    # and keep it busy (untimed) until a sample after the timed region lands
+    t_end = time.time() + 3.0
+    n1 = sampler.count()
+    while sampler.proc is not None and sampler.count() < n1 + 1 and time.time() < t_end:
+        for i in range(4):
+            step(i)
+        torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
 
     # ---- per-step device time of the dominant kernel(s), for the roofline: a
     # separate pass, because events between steps add a few microseconds each
@@ -437,14 +459,22 @@ def run_ours(args, rank, world, local_rank):
     kernel_ms = statistics.median(step_ms)
     achieved = work_per_step / (kernel_ms / 1e3) / scale
     if bound == "tensor":
-        pk = peaks["bf16_tflops"]
+        # the burst GEMM figure for a kernel running at full clock, the sustained
+        # one when the timed region ran under the power cap
+        capped = "sw_power_cap" in clocks.get("reasons", []) or (
+            clocks.get("sm_mhz") and clocks.get("sm_max_mhz")
+            and clocks["sm_mhz"] < 0.9 * clocks["sm_max_mhz"])
+        sustained = capped and peaks.get("bf16_tflops_sustained")
+        pk = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+        peak_kind = " (sustained)" if sustained else " (burst)"
         runit = "TFLOP/s"
     else:
         pk = peaks["hbm_gbs"]
+        peak_kind = ""
         runit = "GB/s"
     roofline = {"bound": bound, "achieved": round(achieved, 2), "peak": pk, "unit": runit,
                 "frac": round(achieved / pk, 4), "traffic": read_traffic(f"config{args.config}"),
-                "peak_source": peaks["source"] + (" (burst)" if bound == "tensor" else ""),
+                "peak_source": peaks["source"] + peak_kind,
                 "kernel": kernel_regex, "launch_ms_median": round(kernel_ms, 5),
                 "note": "achieved = algorithmic work per step / median per-step device time "
                         "(CUDA events on the launching stream)"}
@@ -515,7 +545,7 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
