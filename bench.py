@@ -4,7 +4,7 @@
 Default workload: BASELINE config 2, the reference's headline shape -- non-causal
 prefill forward, B=1, H=8, N=4096, D=64, fp16, returning O and L
 (bench/bench_fa3_headline.py of the reference times the same call, forward()+L).
-A step is one forward over one batch.  Other configs: --config 1|2|3|4|4s|5a.
+A step is one forward over one batch.  Other configs: --config 1|2|3|3s|4|4s|5a|5b.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
 
@@ -48,6 +48,9 @@ CONFIGS = {
               shard=False, name="config2: prefill fwd B=1 H=8 N=4096 D=64 fp16 non-causal"),
     "3": dict(kind="prefill", B=4, H=32, Hkv=32, N=8192, D=128, dtype="bfloat16", causal=True,
               shard=True, name="config3: prefill fwd B=4 H=32 N=8192 D=128 bf16 causal"),
+    # config 3 at 1/4 of the heads (201 MB of Q/K/V, still > L2): the case ncu section captures run on
+    "3s": dict(kind="prefill", B=1, H=32, Hkv=32, N=8192, D=128, dtype="bfloat16", causal=True,
+               shard=True, name="config3-small: prefill fwd B=1 H=32 N=8192 D=128 bf16 causal"),
     "4": dict(kind="decode", B=64, H=32, Hkv=8, L=16384, D=128, dtype="float16", splits=16,
               shard=True, name="config4: split-KV GQA decode B=64 H=32 Hkv=8 L=16384 D=128 fp16"),
     # config 4 at 1/8 batch (537 MB of KV, still > L2): the case ncu section captures run on
@@ -234,7 +237,7 @@ def run_ours(args, rank, world, local_rank):
             q, k, v = sets[i % nsets]
             return b200attn.forward(q, k, v, causal=c["causal"])
 
-        kernel_regex = "prefill_fwd_kernel"
+        kernel_regex = "prefill_d64_kernel" if c["D"] == 64 else "prefill_fwd_kernel"
         bound, peak = "tensor", None
         h2d = 3 * int(np.prod(shape)) * 2
         d2h = int(np.prod(shape)) * 2 + int(np.prod(shape[:3])) * 4
