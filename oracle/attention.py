@@ -168,3 +168,42 @@ def seeded_normal(shape, seed, amp=1.0):
     """N(0,1)*amp float32 values from a seeded generator (device-independent bits)."""
     rng = np.random.default_rng(seed)
     return (rng.standard_normal(shape, dtype=np.float32) * np.float32(amp))
+
+
+# ---------------------------------------------------------------------- backward
+
+def attention_backward(Q, K, V, dO, scale=None, causal=False, dtype=np.float64):
+    """(dQ, dK, dV) of O = softmax(Q K^T * scale) V for upstream gradient dO.
+
+    Restates the reference's naive backward (tests/test_backward.py:20-46) and
+    the kernels it checks (cuda/flash_attn_kernel.cu:173-412):
+        P = softmax(S);  dV = P^T dO;  dP = dO V^T;  D_i = rowsum(dO * O);
+        dS = P * (dP - D_i);  dQ = dS K * scale;  dK = dS^T Q * scale
+    with the same causal mask (aligned to the last key) and GQA head sharing as
+    naive_attention: dK/dV of a KV head sum over the query heads that use it.
+    """
+    B, H, N, D = Q.shape
+    Hkv, Nk = K.shape[1], K.shape[2]
+    scale = D ** -0.5 if scale is None else scale
+    dQ = np.zeros((B, H, N, D), dtype=dtype)
+    dK = np.zeros((B, Hkv, Nk, D), dtype=dtype)
+    dV = np.zeros((B, Hkv, Nk, D), dtype=dtype)
+    for b in range(B):
+        for h in range(H):
+            hk = _kv_head(h, H, Hkv)
+            q, k, v, do = (np.asarray(x, dtype=dtype) for x in (Q[b, h], K[b, hk], V[b, hk], dO[b, h]))
+            s = (q @ k.T) * dtype(scale)
+            if causal:
+                rows = np.arange(N)[:, None] + (Nk - N)
+                s = np.where(np.arange(Nk)[None, :] <= rows, s, -np.inf)
+            m = s.max(axis=-1, keepdims=True)
+            p = np.exp(s - m)
+            p /= p.sum(axis=-1, keepdims=True)
+            o = p @ v
+            dV[b, hk] += p.T @ do
+            dp = do @ v.T
+            di = (do * o).sum(axis=-1, keepdims=True)
+            ds = p * (dp - di)
+            dQ[b, h] = ds @ k * scale
+            dK[b, hk] += ds.T @ q * scale
+    return dQ, dK, dV

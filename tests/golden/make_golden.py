@@ -6,7 +6,8 @@ the CPU, in fp32, on seeded inputs -- the inputs are half-cast first, as the
 reference's tests do (tests/test_fa3_db_full.py:28-35).  The shape grid is the
 reference's own (tests/test_fa3_db_full.py:58-75: full-tile and guarded N,
 B=2/H=4, amp=16 stress), plus D=128, bf16-cast inputs, and query-length-1
-(decode) cases that the same function evaluates unchanged.
+(decode) cases that the same function evaluates unchanged, and backward
+cases from the reference's naive backward (tests/test_backward.py:20-46).
 
 Inputs are stored as raw 16-bit patterns (q, k, v as uint16, with `dtype`
 naming float16 or bfloat16); O and L as float32.  The fixtures are committed;
@@ -32,6 +33,20 @@ def load_reference(ref_root: str):
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     return mod.naive_attention
+
+
+def load_reference_backward(ref_root: str):
+    """The reference's naive backward, tests/test_backward.py:20-46.  That file
+    imports a compiled extension at module level, so only the two naive
+    functions' source is executed (unchanged), not the module."""
+    import ast
+    path = os.path.join(ref_root, "tests", "test_backward.py")
+    tree = ast.parse(open(path).read())
+    keep = [n for n in tree.body if isinstance(n, ast.FunctionDef)
+            and n.name in ("naive_attention_forward", "naive_attention_backward")]
+    ns = {"torch": torch}
+    exec(compile(ast.Module(body=keep, type_ignores=[]), path, "exec"), ns)
+    return ns["naive_attention_backward"]
 
 
 def inputs(shape_q, shape_kv, seed, amp, dtype):
@@ -62,6 +77,14 @@ DECODE_CASES = [
 ]
 
 
+BACKWARD_CASES = [
+    # (name, B, H, N, D, dtype) -- small cases from the reference's backward grid
+    # (tests/test_backward.py:95-105: N 32..2048 at D=64) plus a D=128 bf16 one
+    ("bwd_n128", 1, 2, 128, 64, torch.float16),
+    ("bwd_n77_d128", 1, 2, 77, 128, torch.bfloat16),
+]
+
+
 def bits(t: torch.Tensor) -> np.ndarray:
     """Raw 16-bit patterns of a half / bfloat16 tensor (lossless, half the size of fp32)."""
     return t.contiguous().view(torch.int16).numpy().view(np.uint16)
@@ -81,7 +104,16 @@ def main(ref_root: str) -> None:
         np.savez_compressed(os.path.join(HERE, f"decode_{name}.npz"),
                             q=bits(q), k=bits(k), v=bits(v), O=O.numpy(), L=L.numpy(),
                             dtype=str(dt).split(".")[-1])
-    print("wrote", len(PREFILL_CASES) + len(DECODE_CASES), "fixtures to", HERE)
+    naive_bwd = load_reference_backward(ref_root)
+    for i, (name, B, H, N, D, dt) in enumerate(BACKWARD_CASES):
+        q, k, v = inputs((B, H, N, D), (B, H, N, D), 3000 + i, 1.0, dt)
+        rng = np.random.default_rng(4000 + i)
+        do = torch.from_numpy(rng.standard_normal((B, H, N, D), dtype=np.float32)).to(dt)
+        dQ, dK, dV = naive_bwd(q.float(), k.float(), v.float(), do.float())
+        np.savez_compressed(os.path.join(HERE, f"backward_{name}.npz"),
+                            q=bits(q), k=bits(k), v=bits(v), do=bits(do), dQ=dQ.numpy(),
+                            dK=dK.numpy(), dV=dV.numpy(), dtype=str(dt).split(".")[-1])
+    print("wrote", len(PREFILL_CASES) + len(DECODE_CASES) + len(BACKWARD_CASES), "fixtures to", HERE)
 
 
 if __name__ == "__main__":

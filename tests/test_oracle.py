@@ -115,3 +115,36 @@ def test_causal_cross_mask_aligned_to_last_key():
     for r in range(5):  # row r sees keys 0 .. r + 4
         o, l = ora.attention_head(q[0, 0, r:r + 1], k[0, 0, :r + 5], v[0, 0, :r + 5], 0.25)
         np.testing.assert_allclose(O[0, 0, r], o[0], rtol=1e-12, atol=1e-12)
+
+
+BACKWARD = golden_files("backward")
+
+
+@pytest.mark.parametrize("path", BACKWARD, ids=lambda p: os.path.basename(p)[:-4])
+def test_oracle_backward_matches_reference(path):
+    from conftest import bits_to_float
+    z = np.load(path)
+    dt = str(z["dtype"])
+    q, k, v, do = (bits_to_float(z[n], dt) for n in ("q", "k", "v", "do"))
+    dQ, dK, dV = ora.attention_backward(q, k, v, do)
+    for ours, ref in ((dQ, z["dQ"]), (dK, z["dK"]), (dV, z["dV"])):
+        np.testing.assert_allclose(ours, ref, atol=1e-4, rtol=1e-4)
+
+
+def test_oracle_backward_matches_finite_differences():
+    q = ora.seeded_normal((1, 2, 6, 8), 30).astype(np.float64)
+    k = ora.seeded_normal((1, 1, 9, 8), 31).astype(np.float64)
+    v = ora.seeded_normal((1, 1, 9, 8), 32).astype(np.float64)
+    do = ora.seeded_normal((1, 2, 6, 8), 33).astype(np.float64)
+    dQ, dK, dV = ora.attention_backward(q, k, v, do, causal=True)
+    f = lambda q_, k_, v_: (ora.naive_attention(q_, k_, v_, causal=True)[0] * do).sum()
+    eps = 1e-6
+    for arr, grad in ((q, dQ), (k, dK), (v, dV)):
+        idx = (0, 0, 3, 5)
+        a1, a2 = arr.copy(), arr.copy()
+        a1[idx] += eps
+        a2[idx] -= eps
+        args1 = [a1 if arr is x else x for x in (q, k, v)]
+        args2 = [a2 if arr is x else x for x in (q, k, v)]
+        num = (f(*args1) - f(*args2)) / (2 * eps)
+        np.testing.assert_allclose(grad[idx], num, rtol=1e-6, atol=1e-8)
