@@ -36,6 +36,9 @@ _SIGNATURES = {
     "b2a_decode_paged_noalloc": (_c_int, [_vp] * 7 + [_c_int] * 8 + [_c_int, _c_float, _vp]),
     # k_new v_new k_pool v_pool bt lens | B Hkv T D page max_pages num_pages dtype advance | stream
     "b2a_kv_append_paged": (_c_int, [_vp] * 6 + [_c_int] * 9 + [_vp]),
+    # q k v o dO lse dq dk dv ws | B H Hkv N Nk D dtype causal | scale stream
+    "b2a_backward": (_c_int, [_vp] * 10 + [_c_int] * 8 + [_c_float, _vp]),
+    "b2a_backward_workspace_floats": (ctypes.c_int64, [_c_int] * 4),
     "b2a_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint32)]),
 }
 

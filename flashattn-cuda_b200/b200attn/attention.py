@@ -89,6 +89,39 @@ def forward_only(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, causal: bool
     return O
 
 
+def backward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, O: torch.Tensor,
+             dO: torch.Tensor, L: torch.Tensor, causal: bool = False,
+             scale: Optional[float] = None) -> list:
+    """Gradients [dQ, dK, dV] of the forward (reference `backward(Q, K, V, O, dO, L)`,
+    cuda/flash_attn_kernel.cu:417-502).  O and L are `forward`'s outputs; dK, dV
+    have K's shape (for GQA they sum over the query heads sharing a KV head)."""
+    for t in (Q, K, V, O, dO, L):
+        if not t.is_cuda:
+            raise RuntimeError("Q/K/V must be CUDA tensors")
+    B, H, N, D = Q.shape
+    Hkv, Nk = K.shape[1], K.shape[2]
+    if D not in (64, 128):
+        raise RuntimeError("Head dimension must be 64 or 128")
+    if O.shape != Q.shape or dO.shape != Q.shape or L.shape != (B, H, N) or V.shape != K.shape:
+        raise RuntimeError("O and dO must have Q's shape, L [B, H, N], V K's shape")
+    dt = _compute_dtype(Q)
+    lib = _lib.load()
+    with torch.cuda.device(Q.device):
+        Qc, Kc, Vc, Oc, dOc = (t.to(dt).contiguous() for t in (Q, K, V, O, dO))
+        Lc = L.float().contiguous()
+        dQ = torch.empty_like(Qc)
+        dK = torch.empty_like(Kc)
+        dV = torch.empty_like(Vc)
+        ws = torch.empty(int(lib.b2a_backward_workspace_floats(B, H, N, D)), dtype=torch.float32,
+                         device=Q.device)
+        s = float(D) ** -0.5 if scale is None else float(scale)
+        _lib.check(lib.b2a_backward(
+            Qc.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), Oc.data_ptr(), dOc.data_ptr(),
+            Lc.data_ptr(), dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), ws.data_ptr(),
+            B, H, Hkv, N, Nk, D, _DT[dt], int(bool(causal)), s, _stream(Q.device)))
+    return [dQ, dK, dV]
+
+
 # ---------------------------------------------------------------------------- decode
 
 def _decode_q(q: torch.Tensor):

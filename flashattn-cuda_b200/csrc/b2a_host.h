@@ -16,12 +16,13 @@ int set_error(int status, const char* msg);
 // Record a CUDA runtime failure ("<what>: <cuda error string>").
 int set_cuda_error(cudaError_t e, const char* what);
 
-// 3-D tiled tensor map over a contiguous [outer, rows, inner] array of 2-byte
-// elements: dims {inner, rows, outer}, box {box_inner, box_rows, 1}.  Rows past
-// `rows` (per outer index) read as zero.
+// 3-D tiled tensor map over a contiguous [outer, rows, inner] array of
+// `elem_bytes`-byte elements: dims {inner, rows, outer}, box {box_inner,
+// box_rows, 1}.  Rows past `rows` (per outer index) read as zero; stores and
+// reductions there are dropped.
 int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner,
                  uint64_t rows, uint64_t outer, uint32_t box_inner, uint32_t box_rows,
-                 bool swizzle128);
+                 bool swizzle128, uint32_t elem_bytes = 2);
 // 2-D tiled tensor map over a contiguous [rows, inner] array of 2-byte elements.
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner,
                  uint64_t rows, uint32_t box_inner, uint32_t box_rows, bool swizzle128);
@@ -30,6 +31,7 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uin
 int take_error_flags_prefill(uint32_t* flags);
 int take_error_flags_prefill_d64(uint32_t* flags);
 int take_error_flags_kvcache(uint32_t* flags);
+int take_error_flags_backward(uint32_t* flags);
 int take_error_flags_decode(uint32_t* flags);
 
 // Defines take_error_flags_<unit>() for the unit that expands it.
@@ -55,6 +57,10 @@ int decode_dispatch(const void* q, const void* k, const void* v, const int32_t* 
                     const int32_t* kv_lens, float* o_part, float* l_part, int B, int H, int Hkv,
                     int Lkv, int D, int splits, int tokens_per_split, int page_size, int max_pages,
                     int num_pages, int dtype, float scale, cudaStream_t stream);
+int backward_dispatch(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                      const float* lse, void* dq, void* dk, void* dv, float* workspace, int B,
+                      int H, int Hkv, int N, int Nk, int D, int dtype, int causal, float scale,
+                      cudaStream_t stream);
 int kv_append_dispatch(const void* k_new, const void* v_new, void* k_pool, void* v_pool,
                        const int32_t* block_table, int32_t* kv_lens, int B, int Hkv, int T, int D,
                        int page_size, int max_pages, int num_pages, int advance,

@@ -123,9 +123,9 @@ static int make_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dt,
 
 int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner,
                  uint64_t rows, uint64_t outer, uint32_t box_inner, uint32_t box_rows,
-                 bool swizzle128) {
+                 bool swizzle128, uint32_t elem_bytes) {
   cuuint64_t dims[3] = {inner, rows, outer};
-  cuuint64_t strides[2] = {inner * 2, inner * rows * 2};
+  cuuint64_t strides[2] = {inner * elem_bytes, inner * rows * elem_bytes};
   cuuint32_t box[3] = {box_inner, box_rows, 1};
   return make_tmap(map, base, dt, 3, dims, strides, box, swizzle128);
 }
@@ -272,6 +272,39 @@ int b2a_decode_paged(const void* q, const void* k_pool, const void* v_pool,
   return combine_dispatch(o_part, l_part, o, lse, B, H, splits, D, dtype, kv_lens, tps, s);
 }
 
+int b2a_backward(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                 const float* lse, void* dq, void* dk, void* dv, float* workspace, int B, int H,
+                 int Hkv, int N, int Nk, int D, int dtype, int causal, float scale, void* stream) {
+  t_last_error[0] = 0;
+  B2A_TRY(common_checks(dtype));
+  if (D != 64 && D != 128) return set_error(B2A_ERR_UNSUPPORTED, "Head dimension must be 64 or 128");
+  if (N <= 0 || Nk <= 0) return set_error(B2A_ERR_INVALID_ARG, "N must be > 0");
+  if (causal && Nk < N)
+    return set_error(B2A_ERR_INVALID_ARG,
+                     "causal attention needs Nk >= N (the mask is aligned to the last key)");
+  if (B <= 0 || H <= 0 || Hkv <= 0) return set_error(B2A_ERR_INVALID_ARG, "B, H and Hkv must be > 0");
+  if (H % Hkv != 0) return set_error(B2A_ERR_INVALID_ARG, "H must be a multiple of Hkv");
+  if ((int64_t)B * Hkv > 65535) return set_error(B2A_ERR_INVALID_ARG, "B*Hkv must be <= 65535");
+  if (!(scale > 0.f)) return set_error(B2A_ERR_INVALID_ARG, "scale must be > 0");
+  B2A_TRY(check_device_ptr(q, "Q"));
+  B2A_TRY(check_device_ptr(k, "K"));
+  B2A_TRY(check_device_ptr(v, "V"));
+  B2A_TRY(check_device_ptr(o, "O"));
+  B2A_TRY(check_device_ptr(dout, "dO"));
+  B2A_TRY(check_device_ptr(lse, "L"));
+  B2A_TRY(check_device_ptr(dq, "dQ"));
+  B2A_TRY(check_device_ptr(dk, "dK"));
+  B2A_TRY(check_device_ptr(dv, "dV"));
+  B2A_TRY(check_device_ptr(workspace, "workspace"));
+  return backward_dispatch(q, k, v, o, dout, lse, dq, dk, dv, workspace, B, H, Hkv, N, Nk, D,
+                           dtype, causal, scale, static_cast<cudaStream_t>(stream));
+}
+
+int64_t b2a_backward_workspace_floats(int B, int H, int N, int D) {
+  const int64_t rows = (int64_t)B * H * N;
+  return ((rows + 63) / 64) * 64 + rows * D;
+}
+
 int b2a_kv_append_paged(const void* k_new, const void* v_new, void* k_pool, void* v_pool,
                         const int32_t* block_table, int32_t* kv_lens, int B, int Hkv, int T,
                         int D, int page_size, int max_pages, int num_pages, int dtype,
@@ -303,6 +336,7 @@ int b2a_device_error(uint32_t* flags) {
   B2A_TRY(take_error_flags_prefill(&v));
   B2A_TRY(take_error_flags_prefill_d64(&v));
   B2A_TRY(take_error_flags_kvcache(&v));
+  B2A_TRY(take_error_flags_backward(&v));
   B2A_TRY(take_error_flags_decode(&v));
   *flags = v;
   return B2A_OK;

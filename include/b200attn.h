@@ -76,6 +76,24 @@ int b2a_prefill_fwd_kv(const void* q, const void* k, const void* v, void* o,
                        int dtype, int causal, float scale, void* stream);
 
 /*
+ * Backward of the prefill forward: dQ [B,H,N,D], dK, dV [B,Hkv,Nk,D] (dtype)
+ * from Q, K, V, the forward's O and lse (natural-log logsumexp, fp32) and the
+ * upstream gradient dO [B,H,N,D]; causal and scale as in the forward.  For
+ * GQA, dK/dV of a KV head sum over its query heads.  `workspace` is
+ * caller-provided fp32 scratch of b2a_backward_workspace_floats(B,H,N,D)
+ * floats (row statistics and the dQ accumulator).  Replaces the reference's
+ * backward(Q, K, V, O, dO, L) -> [dQ, dK, dV]
+ * (cuda/flash_attn_kernel.cu:417-502 with the kernels at :173-412).
+ */
+int b2a_backward(const void* q, const void* k, const void* v, const void* o,
+                 const void* dout, const float* lse, void* dq, void* dk,
+                 void* dv, float* workspace, int B, int H, int Hkv, int N,
+                 int Nk, int D, int dtype, int causal, float scale,
+                 void* stream);
+/* Floats of workspace b2a_backward needs. */
+int64_t b2a_backward_workspace_floats(int B, int H, int N, int D);
+
+/*
  * Split-KV decode, first stage: for each (batch, query head, split) the
  * softmax-normalised partial output and its natural-log sum of exp.  The KV
  * sequence of length Lkv is cut into `splits` chunks of ceil(Lkv/splits)
