@@ -246,13 +246,11 @@ def run_ours(args, rank, world, local_rank):
         host_out = (torch.empty(shape, dtype=tdt).pin_memory(),
                     torch.empty(shape[:3], dtype=torch.float32).pin_memory())
 
-        def e2e_step(i):
-            q = host_in[0].to(dev, non_blocking=True)
-            k = host_in[1].to(dev, non_blocking=True)
-            v = host_in[2].to(dev, non_blocking=True)
-            O, L = b200attn.forward(q, k, v, causal=c["causal"])
-            host_out[0].copy_(O, non_blocking=True)
-            host_out[1].copy_(L, non_blocking=True)
+        e2e_in = host_in
+        static_out = False
+
+        def e2e_run(q, k, v):
+            return b200attn.forward(q, k, v, causal=c["causal"])
 
         workload = dict(workload=c["name"], B=Bl, H=Hl, N=c["N"], D=c["D"],
                         causal=c["causal"], dtype=c["dtype"], units_per_rank=Bl * Hl)
@@ -284,11 +282,11 @@ def run_ours(args, rank, world, local_rank):
         host_out = (torch.empty(B, H, 1, D, dtype=tdt).pin_memory(),
                     torch.empty(B, H, 1, dtype=torch.float32).pin_memory())
 
-        def e2e_step(i):
-            qd = host_q.to(dev, non_blocking=True)
-            O, Lo = cap(qd) if args.graph else b200attn.decode(qd, k, v, splits=c["splits"])
-            host_out[0].copy_(O, non_blocking=True)
-            host_out[1].copy_(Lo, non_blocking=True)
+        e2e_in = [host_q]
+        static_out = bool(args.graph)
+
+        def e2e_run(qd):
+            return cap(qd) if args.graph else b200attn.decode(qd, k, v, splits=c["splits"])
 
         workload = dict(workload=c["name"], B=B, H=H, Hkv=Hkv, L=L, D=D, splits=c["splits"],
                         dtype=c["dtype"], kv_cache="resident (4.3 GB/step > L2)")
@@ -322,11 +320,11 @@ def run_ours(args, rank, world, local_rank):
         host_out = (torch.empty(B, H, 1, D, dtype=tdt).pin_memory(),
                     torch.empty(B, H, 1, dtype=torch.float32).pin_memory())
 
-        def e2e_step(i):
-            qd = host_q.to(dev, non_blocking=True)
-            O, Lo = cap(qd) if args.graph else decode_kv_sharded(qd, k, v, splits=c["splits"])
-            host_out[0].copy_(O, non_blocking=True)
-            host_out[1].copy_(Lo, non_blocking=True)
+        e2e_in = [host_q]
+        static_out = bool(args.graph)
+
+        def e2e_run(qd):
+            return cap(qd) if args.graph else decode_kv_sharded(qd, k, v, splits=c["splits"])
 
         workload = dict(workload=c["name"], B=B, H=H, Hkv=Hkv, L=c["L"], L_per_rank=Ll, D=D,
                         splits_per_rank=c["splits"], dtype=c["dtype"],
@@ -374,11 +372,11 @@ def run_ours(args, rank, world, local_rank):
         host_out = (torch.empty(B, H, 1, D, dtype=tdt).pin_memory(),
                     torch.empty(B, H, 1, dtype=torch.float32).pin_memory())
 
-        def e2e_step(i):
-            qd = host_q.to(dev, non_blocking=True)
-            O, Lo = b200attn.decode_paged(qd, kp, vp, bt, kl, pages_per_split=c["pps"])
-            host_out[0].copy_(O, non_blocking=True)
-            host_out[1].copy_(Lo, non_blocking=True)
+        e2e_in = [host_q]
+        static_out = False
+
+        def e2e_run(qd):
+            return b200attn.decode_paged(qd, kp, vp, bt, kl, pages_per_split=c["pps"])
 
         workload = dict(workload=c["name"], B=B, total_tokens=int(lens.sum()),
                         pages=P, pages_per_split=c["pps"], dtype=c["dtype"])
@@ -433,16 +431,49 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     step_ms = [a.elapsed_time(b) for a, b in kev]
 
-    # ---- end-to-end through the public API with host buffers
-    for i in range(2):
-        e2e_step(i)
+    # ---- end-to-end through the public API with host buffers.  Every step copies
+    # its inputs host->device and its outputs device->host inside the timed
+    # region; the copies run on their own streams, double-buffered, so that
+    # step i+1's upload and step i-1's download overlap step i's compute.
+    cp_in = torch.cuda.Stream(dev)
+    cp_out = torch.cuda.Stream(dev)
+    slots = [[torch.empty_like(h, device=dev) for h in e2e_in] for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_loop(n):
+        for i in range(n):
+            sl = i % 2
+            with torch.cuda.stream(cp_in):
+                if i >= 2:
+                    cp_in.wait_event(ev_done[sl])  # slot's inputs consumed by step i-2
+                for d, hsrc in zip(slots[sl], e2e_in):
+                    d.copy_(hsrc, non_blocking=True)
+                ev_in[sl].record(cp_in)
+            stream.wait_event(ev_in[sl])
+            if static_out and i >= 1:
+                stream.wait_event(ev_out[(i - 1) % 2])  # graph outputs are reused
+            outs = e2e_run(*slots[sl])
+            ev_done[sl].record(stream)
+            with torch.cuda.stream(cp_out):
+                cp_out.wait_event(ev_done[sl])
+                for o, hdst in zip(outs, host_out):
+                    hdst.copy_(o, non_blocking=True)
+                    o.record_stream(cp_out)
+                ev_out[sl].record(cp_out)
+        stream.wait_stream(cp_in)
+        stream.wait_stream(cp_out)
+
+    e2e_loop(3)
     torch.cuda.synchronize(dev)
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
-        e2e_step(i)
+    cp_in.wait_event(e0)
+    cp_out.wait_event(e0)
+    e2e_loop(args.steps)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1)
