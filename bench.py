@@ -62,7 +62,16 @@ CONFIGS = {
     "5a": dict(kind="paged", B=128, H=32, Hkv=8, D=128, page=16, lmin=512, lmax=32768,
                dtype="float16", pps=64, shard=True,
                name="config5a: paged decode B=128 H=32 Hkv=8 D=128 fp16 page=16 len U[512,32768]"),
+    "6": dict(kind="varlen", B=16, H=32, Hkv=8, D=128, lmin=256, lmax=8192, dtype="bfloat16",
+              causal=True, shard=True,
+              name="varlen prefill fwd: 16 packed sequences len U[256,8192] H=32 Hkv=8 D=128 "
+                   "bf16 causal"),
 }
+
+
+def varlen_lengths(c):
+    rng = np.random.default_rng(66)
+    return rng.integers(c["lmin"], c["lmax"] + 1, size=c["B"]).astype(np.int64)
 
 
 def prefill_flops(c, units):
@@ -164,9 +173,11 @@ def cpu_sample(cfg_key: str, steps: int, warmup: int):
     from oracle import attention as ora
     c = CONFIGS[cfg_key]
     cores = os.cpu_count() or 1
-    if c["kind"] == "prefill":
-        # one (b, h) head per step (rows limited for the causal N=8192 case)
-        N, D = c["N"], c["D"]
+    if c["kind"] in ("prefill", "varlen"):
+        # one (b, h) head per step (rows limited for the causal N=8192 case);
+        # varlen: one head of a sequence of the median length
+        N = c["N"] if c["kind"] == "prefill" else int(np.median(varlen_lengths(c)))
+        D = c["D"]
         rows = min(N, 2048)
         q = ora.seeded_normal((rows, D), 1)
         k = ora.seeded_normal((N, D), 2)
@@ -254,6 +265,54 @@ def run_ours(args, rank, world, local_rank):
 
         workload = dict(workload=c["name"], B=Bl, H=Hl, N=c["N"], D=c["D"],
                         causal=c["causal"], dtype=c["dtype"], units_per_rank=Bl * Hl)
+    elif c["kind"] == "varlen":
+        lens_all = varlen_lengths(c)
+        # greedy balance of sequences over ranks by attention work (~ n^2)
+        order = np.argsort(-lens_all)
+        loads = [0] * world
+        mine = []
+        for idx in order:
+            r = int(np.argmin(loads))
+            loads[r] += int(lens_all[idx]) ** 2
+            if r == rank:
+                mine.append(idx)
+        lens = lens_all[sorted(mine)]
+        H, Hkv, D = c["H"], c["Hkv"], c["D"]
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32)
+        T, maxlen = int(lens.sum()), int(lens.max())
+        q = torch.randn(T, H, D, device=dev, generator=gen).to(tdt)
+        k = torch.randn(T, Hkv, D, device=dev, generator=gen).to(tdt)
+        v = torch.randn(T, Hkv, D, device=dev, generator=gen).to(tdt)
+        cud = cu.to(dev)
+        nsets = 1  # 550 MB of Q/K/V per step on one rank, well past L2
+        # causal with Nk == N: each (sequence, head) does 2*D*n*(n+1) FLOPs
+        work_per_step = sum(2 * D * int(n) * (int(n) + 1) for n in lens) * H
+        unit = "TFLOP/s"
+
+        def step(i):
+            return b200attn.forward_varlen(q, k, v, cud, cud, maxlen, causal=c["causal"])
+
+        kernel_regex = "prefill_fwd_kernel"
+        bound, peak = "tensor", None
+        h2d = (T * H * D + 2 * T * Hkv * D) * 2 + 2 * cu.numel() * 4
+        d2h = T * H * D * 2 + H * T * 4
+        hg = torch.Generator().manual_seed(rank)
+        host_in = [torch.randn(T, H, D, generator=hg).to(tdt).pin_memory(),
+                   torch.randn(T, Hkv, D, generator=hg).to(tdt).pin_memory(),
+                   torch.randn(T, Hkv, D, generator=hg).to(tdt).pin_memory(),
+                   cu.pin_memory(), cu.clone().pin_memory()]
+        host_out = (torch.empty(T, H, D, dtype=tdt).pin_memory(),
+                    torch.empty(H, T, dtype=torch.float32).pin_memory())
+
+        e2e_in = host_in
+        static_out = False
+
+        def e2e_run(q, k, v, cq, ck):
+            return b200attn.forward_varlen(q, k, v, cq, ck, maxlen, causal=c["causal"])
+
+        workload = dict(workload=c["name"], sequences=len(lens), total_tokens=T,
+                        max_seqlen=maxlen, H=H, Hkv=Hkv, D=D, causal=c["causal"],
+                        dtype=c["dtype"])
     elif c["kind"] == "decode":
         B = c["B"] // world if c["shard"] else c["B"]
         H, Hkv, L, D = c["H"], c["Hkv"], c["L"], c["D"]
@@ -520,7 +579,7 @@ def run_ours(args, rank, world, local_rank):
             v, u, sample, cores = cpu_sample(args.config, steps=2, warmup=1)
             cpu = {"value": round(v, 6), "unit": u, "cores": cores, "kind": "port",
                    "sample": sample}
-        kernel_launches = args.steps * (1 if c["kind"] == "prefill" else 2)  # timed region only
+        kernel_launches = args.steps * (1 if c["kind"] in ("prefill", "varlen") else 2)  # timed region only
         out = {
             "metric": METRIC,
             "value": round(value, 3),

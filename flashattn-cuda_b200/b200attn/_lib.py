@@ -26,6 +26,8 @@ _SIGNATURES = {
     # q k v o lse | B H Hkv N Nk D | dtype causal scale stream
     "b2a_prefill_fwd_kv": (_c_int, [_vp, _vp, _vp, _vp, _vp] + [_c_int] * 6
                            + [_c_int, _c_int, _c_float, _vp]),
+    # q k v o lse cu_q cu_k | B H Hkv total_q total_k max_seqlen_q D | dtype causal scale stream
+    "b2a_prefill_fwd_varlen": (_c_int, [_vp] * 7 + [_c_int] * 7 + [_c_int, _c_int, _c_float, _vp]),
     # q k v o_part l_part | B H Hkv Lkv D splits | dtype scale stream
     "b2a_decode_splitkv": (_c_int, [_vp] * 5 + [_c_int] * 6 + [_c_int, _c_float, _vp]),
     # o_part l_part o lse | B H splits D dtype | stream

@@ -12,8 +12,8 @@ under a device guard (:365, :380).
 Additions over the reference, all opt-in: bf16 inputs compute and return bf16
 (the reference would cast them to fp16), D = 128, `causal=True`, an explicit
 `scale`, GQA (K/V with fewer heads than Q), a key length Nk different from
-the query length N (causal masks aligned to the last key), and the decode
-entry points
+the query length N (causal masks aligned to the last key), variable-length
+batches packed token-major (`forward_varlen`), and the decode entry points
 `decode_splitkv`, `decode_combine`, `decode` and `decode_paged`.
 """
 from __future__ import annotations
@@ -87,6 +87,58 @@ def forward_only(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, causal: bool
     """Attention forward returning O only (reference `forward_only`); bitwise equal to forward's O."""
     O, _ = _prefill(Q, K, V, False, causal, scale)
     return O
+
+
+def forward_varlen(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
+                   cu_seqlens_q: torch.Tensor, cu_seqlens_k: torch.Tensor, max_seqlen_q: int,
+                   causal: bool = False, scale: Optional[float] = None,
+                   want_L: bool = True) -> list:
+    """Variable-length attention forward over sequences packed token-major.
+
+    Q [total_q, H, D], K/V [total_k, Hkv, D]; cu_seqlens_q / cu_seqlens_k are
+    int32 prefix sums [B+1] starting at 0 (sequence b owns query tokens
+    cu_seqlens_q[b] .. cu_seqlens_q[b+1]-1 and the matching keys).
+    max_seqlen_q must bound every query length.  Returns [O [total_q, H, D],
+    L [H, total_q]] (L is None with want_L=False).  The causal mask is aligned
+    per sequence to its last key; a query row that sees no key gets O = 0 and
+    L = -inf.  The reference has no varlen form (it requires K and V to have
+    Q's shape, cuda/flash_attn_fa3_db_full.cu:358-359).
+    """
+    for t in (Q, K, V, cu_seqlens_q, cu_seqlens_k):
+        if not t.is_cuda:
+            raise RuntimeError("Q/K/V must be CUDA tensors")
+        if t.device != Q.device:
+            raise RuntimeError("Q/K/V must be on the same device")
+    if Q.dim() != 3 or K.dim() != 3 or K.shape != V.shape:
+        raise RuntimeError("varlen Q must be [total_q, H, D] and K, V [total_k, Hkv, D]")
+    total_q, H, D = Q.shape
+    total_k, Hkv, Dk = K.shape
+    if D not in (64, 128):
+        raise RuntimeError("Head dimension must be 64 or 128")
+    if Dk != D or Hkv <= 0 or H % Hkv != 0:
+        raise RuntimeError("K and V must have Q's head dimension and a KV head count dividing H")
+    if (cu_seqlens_q.dim() != 1 or cu_seqlens_q.shape != cu_seqlens_k.shape
+            or cu_seqlens_q.numel() < 2):
+        raise RuntimeError("cu_seqlens_q and cu_seqlens_k must both be [B+1]")
+    if cu_seqlens_q.dtype != torch.int32 or cu_seqlens_k.dtype != torch.int32:
+        raise RuntimeError("cu_seqlens must be int32")
+    B = cu_seqlens_q.numel() - 1
+    dt = _compute_dtype(Q)
+    lib = _lib.load()
+    with torch.cuda.device(Q.device):
+        Qc = Q.to(dt).contiguous()
+        Kc = K.to(dt).contiguous()
+        Vc = V.to(dt).contiguous()
+        cq = cu_seqlens_q.contiguous()
+        ck = cu_seqlens_k.contiguous()
+        O = torch.empty((total_q, H, D), dtype=dt, device=Q.device)
+        L = torch.empty((H, total_q), dtype=torch.float32, device=Q.device) if want_L else None
+        s = float(D) ** -0.5 if scale is None else float(scale)
+        _lib.check(lib.b2a_prefill_fwd_varlen(
+            Qc.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), O.data_ptr(), _ptr(L),
+            cq.data_ptr(), ck.data_ptr(), B, H, Hkv, total_q, total_k, int(max_seqlen_q), D,
+            _DT[dt], int(bool(causal)), s, _stream(Q.device)))
+    return [O, L]
 
 
 def backward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, O: torch.Tensor,

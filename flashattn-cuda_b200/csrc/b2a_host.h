@@ -23,6 +23,12 @@ int set_cuda_error(cudaError_t e, const char* what);
 int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner,
                  uint64_t rows, uint64_t outer, uint32_t box_inner, uint32_t box_rows,
                  bool swizzle128, uint32_t elem_bytes = 2);
+// 3-D tiled tensor map over a packed token-major [tokens, heads, inner] array
+// of 2-byte elements (the varlen layout): dims {inner, heads, tokens}, box
+// {box_inner, 1, box_tokens}, 128-byte swizzle.  A box lands in shared memory
+// as box_tokens rows of box_inner elements, like a make_tmap_3d box.
+int make_tmap_tokens(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner,
+                     uint64_t heads, uint64_t tokens, uint32_t box_inner, uint32_t box_tokens);
 // 2-D tiled tensor map over a contiguous [rows, inner] array of 2-byte elements.
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner,
                  uint64_t rows, uint32_t box_inner, uint32_t box_rows, bool swizzle128);
@@ -50,6 +56,10 @@ int take_error_flags_decode(uint32_t* flags);
 int prefill_dispatch(const void* q, const void* k, const void* v, void* o, float* lse, int B,
                      int H, int Hkv, int N, int Nk, int D, int dtype, int causal, float scale,
                      cudaStream_t stream);
+int prefill_varlen_dispatch(const void* q, const void* k, const void* v, void* o, float* lse,
+                            const int* cu_q, const int* cu_k, int B, int H, int Hkv, int total_q,
+                            int total_k, int max_seqlen_q, int D, int dtype, int causal,
+                            float scale, cudaStream_t stream);
 int prefill_d64_dispatch(const void* q, const void* k, const void* v, void* o, float* lse, int B,
                          int H, int Hkv, int N, int Nk, int dtype, int causal, float scale,
                          cudaStream_t stream);

@@ -34,7 +34,7 @@ int device_ok() {
 
 // A pointer the current device can address as device memory (the C-level
 // counterpart of the reference's "must be CUDA tensors" / "same device").
-int check_device_ptr(const void* p, const char* what) {
+int check_device_ptr(const void* p, const char* what, bool need16 = true) {
   if (p == nullptr) {
     char buf[256];
     snprintf(buf, sizeof buf, "%s must not be null", what);
@@ -56,7 +56,7 @@ int check_device_ptr(const void* p, const char* what) {
   if (attr.type == cudaMemoryTypeDevice && attr.device != dev) {
     return set_error(B2A_ERR_INVALID_ARG, "Q/K/V must be on the same device");
   }
-  if (!aligned16(p)) {
+  if (need16 && !aligned16(p)) {
     char buf[256];
     snprintf(buf, sizeof buf, "%s must be 16-byte aligned", what);
     return set_error(B2A_ERR_MISALIGNED, buf);
@@ -130,6 +130,14 @@ int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uin
   return make_tmap(map, base, dt, 3, dims, strides, box, swizzle128);
 }
 
+int make_tmap_tokens(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner,
+                     uint64_t heads, uint64_t tokens, uint32_t box_inner, uint32_t box_tokens) {
+  cuuint64_t dims[3] = {inner, heads, tokens};
+  cuuint64_t strides[2] = {inner * 2, inner * heads * 2};
+  cuuint32_t box[3] = {box_inner, 1, box_tokens};
+  return make_tmap(map, base, dt, 3, dims, strides, box, true);
+}
+
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner,
                  uint64_t rows, uint32_t box_inner, uint32_t box_rows, bool swizzle128) {
   cuuint64_t dims[2] = {inner, rows};
@@ -188,6 +196,39 @@ int b2a_prefill_fwd_kv(const void* q, const void* k, const void* v, void* o, flo
 int b2a_prefill_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H,
                     int Hkv, int N, int D, int dtype, int causal, float scale, void* stream) {
   return b2a_prefill_fwd_kv(q, k, v, o, lse, B, H, Hkv, N, N, D, dtype, causal, scale, stream);
+}
+
+int b2a_prefill_fwd_varlen(const void* q, const void* k, const void* v, void* o, float* lse,
+                           const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int B, int H,
+                           int Hkv, int total_q, int total_k, int max_seqlen_q, int D, int dtype,
+                           int causal, float scale, void* stream) {
+  t_last_error[0] = 0;
+  B2A_TRY(common_checks(dtype));
+  if (D != 64 && D != 128) return set_error(B2A_ERR_UNSUPPORTED, "Head dimension must be 64 or 128");
+  if (B <= 0 || H <= 0 || Hkv <= 0) return set_error(B2A_ERR_INVALID_ARG, "B, H and Hkv must be > 0");
+  if (H % Hkv != 0) return set_error(B2A_ERR_INVALID_ARG, "H must be a multiple of Hkv");
+  if (total_q <= 0 || total_k <= 0 || max_seqlen_q <= 0)
+    return set_error(B2A_ERR_INVALID_ARG, "total_q, total_k and max_seqlen_q must be > 0");
+  if (max_seqlen_q > total_q)
+    return set_error(B2A_ERR_INVALID_ARG, "max_seqlen_q must be <= total_q");
+  if ((int64_t)B * H > 0x7fffffff) return set_error(B2A_ERR_INVALID_ARG, "B*H too large");
+  if ((max_seqlen_q + 255) / 256 > 65535)
+    return set_error(B2A_ERR_INVALID_ARG, "max_seqlen_q too large (grid.y limit)");
+  if ((int64_t)total_q * H > 0x7fffffff || (int64_t)total_k * Hkv > 0x7fffffff)
+    return set_error(B2A_ERR_INVALID_ARG, "total tokens x heads too large");
+  if (!(scale > 0.f)) return set_error(B2A_ERR_INVALID_ARG, "scale must be > 0");
+  B2A_TRY(check_device_ptr(q, "Q"));
+  B2A_TRY(check_device_ptr(k, "K"));
+  B2A_TRY(check_device_ptr(v, "V"));
+  B2A_TRY(check_device_ptr(o, "O"));
+  if (lse != nullptr) B2A_TRY(check_device_ptr(lse, "L"));
+  B2A_TRY(check_device_ptr(cu_seqlens_q, "cu_seqlens_q", false));
+  B2A_TRY(check_device_ptr(cu_seqlens_k, "cu_seqlens_k", false));
+  if ((reinterpret_cast<uintptr_t>(cu_seqlens_q) | reinterpret_cast<uintptr_t>(cu_seqlens_k)) & 3u)
+    return set_error(B2A_ERR_MISALIGNED, "cu_seqlens must be 4-byte aligned");
+  return prefill_varlen_dispatch(q, k, v, o, lse, cu_seqlens_q, cu_seqlens_k, B, H, Hkv, total_q,
+                                 total_k, max_seqlen_q, D, dtype, causal, scale,
+                                 static_cast<cudaStream_t>(stream));
 }
 
 int b2a_decode_splitkv(const void* q, const void* k, const void* v, float* o_part, float* l_part,

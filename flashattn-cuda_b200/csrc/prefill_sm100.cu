@@ -21,6 +21,16 @@
 //     (the reference packs P into registers, :286-293).  At the end it
 //     normalises O_t by the row sum and writes O and L = m ln2 + ln l (:340).
 //
+// VARLEN: sequences of different lengths packed token-major, q [total_q, H,
+// D] and k/v [total_k, Hkv, D], sequence b owning tokens cu_q[b] ..
+// cu_q[b+1]-1 (and cu_k[b] .. cu_k[b+1]-1 of the keys).  The tensor maps are
+// then {D, heads, total} with box {64, 1, 128}: a box lands in shared memory
+// as the same 128 rows x 128 bytes as a {D, N, B*H} box, so the rest of the
+// kernel is unchanged.  A tile that runs past its sequence reads the next
+// sequence's rows: keys there are masked like keys past Nk, query rows there
+// are not stored.  The causal mask is aligned per sequence to its last key;
+// a query row that sees no key gets O = 0 and L = -inf.
+//
 // The two Q tiles ping-pong: while one warpgroup runs its softmax the tensor
 // core runs the other tile's PV and next S, so the MUFU/FMA work of the
 // softmax and the UMMA work overlap.
@@ -67,12 +77,13 @@ struct Cfg {
   static constexpr uint32_t kTmemO = 256;                         // O_t at kTmemO + t*D
 };
 
-template <int D, bool BF16, bool CAUSAL>
+template <int D, bool BF16, bool CAUSAL, bool VARLEN>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, void* __restrict__ out,
-                       float* __restrict__ lse, int N, int Nk, int H, int group, float scale_log2) {
+                       float* __restrict__ lse, int N, int Nk, int H, int group, float scale_log2,
+                       const int* __restrict__ cu_q, const int* __restrict__ cu_k, int total_q) {
   using C = Cfg<D>;
   using E = Elem<BF16>;
   constexpr int S = C::kStages;
@@ -103,9 +114,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int bh = blockIdx.x;
-  const int bhk = (bh / H) * (H / group) + (bh % H) / group;  // KV head of this query head
   const int qb = (int)gridDim.y - 1 - (int)blockIdx.y;
   const int q0 = qb * kRowsPerCta;
+  // tensor-map coordinates: (row, head) of a Q tile / KV tile
+  //   dense  {D, N, B*H}:     y = row, z = b*H + h
+  //   varlen {D, H, total}:   y = h,   z = first token of the sequence + row
+  int q_first = 0, k_first = 0;  // first token of this sequence (varlen)
+  int q_head = bh, k_head = (bh / H) * (H / group) + (bh % H) / group;
+  if constexpr (VARLEN) {
+    const int b = bh / H;
+    q_first = cu_q[b];
+    k_first = cu_k[b];
+    N = cu_q[b + 1] - q_first;
+    Nk = cu_k[b + 1] - k_first;
+    q_head = bh % H;
+    k_head = q_head / group;
+    if (blockIdx.y == 0 && threadIdx.x == 0 && (N > (int)gridDim.y * kRowsPerCta || N < 0 || Nk < 0))
+      atomicOr(&g_error_flags, 8u);  // sequence longer than max_seqlen_q, or bad cu_seqlens
+    if (q0 >= N) return;  // whole CTA: this sequence is shorter
+  }
+  auto tile_y = [&](int row, int head, int first) { return VARLEN ? head : row; };
+  auto tile_z = [&](int row, int head, int first) { return VARLEN ? first + row : head; };
   // keys: Nk (>= N when causal); the causal mask is aligned to the bottom
   // right, query row r sees keys <= r + (Nk - N)
   const int koff = Nk - N;
@@ -113,8 +142,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // KV tiles Q tile t needs (t = 0, 1); the loop runs to the larger one
   int nkv_t[kQTiles];
 #pragma unroll
-  for (int t = 0; t < kQTiles; ++t)
+  for (int t = 0; t < kQTiles; ++t) {
     nkv_t[t] = CAUSAL ? min(nkv_all, (q0 + (t + 1) * BM + koff + BN - 1) / BN) : nkv_all;
+    // varlen: a tile whose rows see no key (Nk == 0, or a causal offset below
+    // zero) still runs one fully masked KV tile, so every role sees >= 1 tile
+    if (VARLEN) nkv_t[t] = max(nkv_t[t], 1);
+  }
   const int nkv = nkv_t[kQTiles - 1];
 
   if (warp == kProducerWarp && lane == 0) {
@@ -150,7 +183,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < kQTiles; ++t)
 #pragma unroll
           for (int c = 0; c < C::kBlocks; ++c)
-            tma_load_3d(sQ + t * C::kQBytes + c * (BM * 128), &tmQ, BAR_Q, c * 64, q0 + t * BM, bh);
+            tma_load_3d(sQ + t * C::kQBytes + c * (BM * 128), &tmQ, BAR_Q, c * 64,
+                        tile_y(q0 + t * BM, q_head, q_first), tile_z(q0 + t * BM, q_head, q_first));
         for (int j = 0; j < nkv; ++j) {
           const int st = j % S;
           if (j >= S && !mbar_wait(BAR_KVE(st), ((j / S) - 1) & 1, abort_flag)) break;
@@ -159,11 +193,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(BAR_KF(st), C::kKVBytes);
 #pragma unroll
           for (int c = 0; c < C::kBlocks; ++c)
-            tma_load_3d(k_dst + c * (BN * 128), &tmK, BAR_KF(st), c * 64, j * BN, bhk);
+            tma_load_3d(k_dst + c * (BN * 128), &tmK, BAR_KF(st), c * 64,
+                        tile_y(j * BN, k_head, k_first), tile_z(j * BN, k_head, k_first));
           mbar_arrive_expect_tx(BAR_VF(st), C::kKVBytes);
 #pragma unroll
           for (int c = 0; c < C::kBlocks; ++c)
-            tma_load_3d(v_dst + c * (BN * 128), &tmV, BAR_VF(st), c * 64, j * BN, bhk);
+            tma_load_3d(v_dst + c * (BN * 128), &tmV, BAR_VF(st), c * 64,
+                        tile_y(j * BN, k_head, k_first), tile_z(j * BN, k_head, k_first));
         }
       }
     } else if (warp == kMmaWarp) {
@@ -322,8 +358,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------- epilogue
     if (ok && mbar_wait(BAR_PVD(t), (my_nkv - 1) & 1, abort_flag)) {
       tc_fence_after();
-      const float inv_l = 1.f / l_run;
-      typename E::T* orow = reinterpret_cast<typename E::T*>(out) + ((size_t)bh * N + grow) * D;
+      // a row that saw no key (varlen only) keeps m_run = -inf: O = 0, L = -inf
+      const bool no_key = VARLEN && m_run == -INFINITY;
+      const float inv_l = no_key ? 0.f : 1.f / l_run;
+      const size_t orow_idx =
+          VARLEN ? ((size_t)(q_first + grow) * H + q_head) : ((size_t)bh * N + grow);
+      typename E::T* orow = reinterpret_cast<typename E::T*>(out) + orow_idx * D;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         float o[32];
@@ -341,8 +381,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (lse != nullptr && grow < N)
-        lse[(size_t)bh * N + grow] = m_run * 0.69314718055994531f + logf(l_run);
+      if (lse != nullptr && grow < N) {
+        // dense L [B, H, N]; varlen L [H, total_q]
+        const size_t li = VARLEN ? ((size_t)q_head * total_q + q_first + grow) : ((size_t)bh * N + grow);
+        // one explicit rounding (fma) so that every instantiation agrees bitwise
+        lse[li] = no_key ? -INFINITY : __fmaf_rn(m_run, 0.69314718055994531f, logf(l_run));
+      }
     }
   }
 
@@ -359,12 +403,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // host launcher
 // ---------------------------------------------------------------------------
-template <int D, bool BF16, bool CAUSAL>
+// Dense: N, Nk are the sequence lengths.  Varlen (cu_q != nullptr): N is
+// max_seqlen_q (it sizes the grid), total_q / total_k the packed token counts.
+template <int D, bool BF16, bool CAUSAL, bool VARLEN>
 static int launch_prefill(const void* q, const void* k, const void* v, void* o, float* lse, int B,
-                          int H, int Hkv, int N, int Nk, float scale, cudaStream_t stream) {
+                          int H, int Hkv, int N, int Nk, float scale, const int* cu_q,
+                          const int* cu_k, int total_q, int total_k, cudaStream_t stream) {
   using namespace prefill;
   using C = Cfg<D>;
-  auto kern = prefill_fwd_kernel<D, BF16, CAUSAL>;
+  auto kern = prefill_fwd_kernel<D, BF16, CAUSAL, VARLEN>;
   static bool attr_done[kMaxDevices] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
@@ -377,15 +424,25 @@ static int launch_prefill(const void* q, const void* k, const void* v, void* o, 
   }
   CUtensorMap tq, tk, tv;
   const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  int rc = make_tmap_3d(&tq, q, dt, D, N, (uint64_t)B * H, 64, BM, /*swizzle128=*/true);
-  if (rc != B2A_OK) return rc;
-  rc = make_tmap_3d(&tk, k, dt, D, Nk, (uint64_t)B * Hkv, 64, BN, true);
-  if (rc != B2A_OK) return rc;
-  rc = make_tmap_3d(&tv, v, dt, D, Nk, (uint64_t)B * Hkv, 64, BN, true);
+  int rc;
+  if (VARLEN) {
+    rc = make_tmap_tokens(&tq, q, dt, D, H, total_q, 64, BM);
+    if (rc != B2A_OK) return rc;
+    rc = make_tmap_tokens(&tk, k, dt, D, Hkv, total_k, 64, BN);
+    if (rc != B2A_OK) return rc;
+    rc = make_tmap_tokens(&tv, v, dt, D, Hkv, total_k, 64, BN);
+  } else {
+    rc = make_tmap_3d(&tq, q, dt, D, N, (uint64_t)B * H, 64, BM, /*swizzle128=*/true);
+    if (rc != B2A_OK) return rc;
+    rc = make_tmap_3d(&tk, k, dt, D, Nk, (uint64_t)B * Hkv, 64, BN, true);
+    if (rc != B2A_OK) return rc;
+    rc = make_tmap_3d(&tv, v, dt, D, Nk, (uint64_t)B * Hkv, 64, BN, true);
+  }
   if (rc != B2A_OK) return rc;
   dim3 grid((unsigned)(B * H), (unsigned)((N + kRowsPerCta - 1) / kRowsPerCta));
   const float scale_log2 = scale * 1.4426950408889634f;
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, o, lse, N, Nk, H, H / Hkv, scale_log2);
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, o, lse, N, Nk, H, H / Hkv, scale_log2,
+                                                  cu_q, cu_k, total_q);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "prefill kernel launch");
   return B2A_OK;
@@ -401,12 +458,36 @@ int prefill_dispatch(const void* q, const void* k, const void* v, void* o, float
   if (D == 64) return prefill_d64_dispatch(q, k, v, o, lse, B, H, Hkv, N, Nk, dtype, causal, scale, stream);
 #define B2A_PF(DD, BB, CC) \
   if (D == DD && bf == BB && (causal != 0) == CC) \
-    return launch_prefill<DD, BB, CC>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, stream);
+    return launch_prefill<DD, BB, CC, false>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, nullptr, \
+                                             nullptr, 0, 0, stream);
   B2A_PF(128, false, false)
   B2A_PF(128, false, true)
   B2A_PF(128, true, false)
   B2A_PF(128, true, true)
 #undef B2A_PF
+  return set_error(B2A_ERR_UNSUPPORTED, "Head dimension must be 64 or 128");
+}
+
+// Varlen prefill, D = 64 or 128 (D = 64 also runs this kernel: the split-row
+// D = 64 kernel has no varlen form).
+int prefill_varlen_dispatch(const void* q, const void* k, const void* v, void* o, float* lse,
+                            const int* cu_q, const int* cu_k, int B, int H, int Hkv, int total_q,
+                            int total_k, int max_seqlen_q, int D, int dtype, int causal,
+                            float scale, cudaStream_t stream) {
+  const bool bf = dtype == B2A_BF16;
+#define B2A_PV(DD, BB, CC)                                                                   \
+  if (D == DD && bf == BB && (causal != 0) == CC)                                            \
+    return launch_prefill<DD, BB, CC, true>(q, k, v, o, lse, B, H, Hkv, max_seqlen_q, 0, scale, \
+                                            cu_q, cu_k, total_q, total_k, stream);
+  B2A_PV(64, false, false)
+  B2A_PV(64, false, true)
+  B2A_PV(64, true, false)
+  B2A_PV(64, true, true)
+  B2A_PV(128, false, false)
+  B2A_PV(128, false, true)
+  B2A_PV(128, true, false)
+  B2A_PV(128, true, true)
+#undef B2A_PV
   return set_error(B2A_ERR_UNSUPPORTED, "Head dimension must be 64 or 128");
 }
 

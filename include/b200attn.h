@@ -76,6 +76,24 @@ int b2a_prefill_fwd_kv(const void* q, const void* k, const void* v, void* o,
                        int dtype, int causal, float scale, void* stream);
 
 /*
+ * Variable-length prefill forward: B sequences packed token-major,
+ * Q,O [total_q, H, D], K,V [total_k, Hkv, D]; sequence b owns query tokens
+ * cu_seqlens_q[b] .. cu_seqlens_q[b+1]-1 and keys cu_seqlens_k[b] ..
+ * cu_seqlens_k[b+1]-1 (int32 device arrays of B+1 prefix sums starting at 0).
+ * lse is [H, total_q] (nullable).  max_seqlen_q bounds every query length (it
+ * sizes the grid; a longer sequence sets bit 3 of the device error word and
+ * its tail rows are not computed).  With causal != 0 the mask is aligned per
+ * sequence to its last key; a query row that sees no key gets O = 0 and
+ * lse = -inf.  The reference has no varlen form: it requires K and V to have
+ * Q's shape (cuda/flash_attn_fa3_db_full.cu:358-359).
+ */
+int b2a_prefill_fwd_varlen(const void* q, const void* k, const void* v, void* o,
+                           float* lse, const int32_t* cu_seqlens_q,
+                           const int32_t* cu_seqlens_k, int B, int H, int Hkv,
+                           int total_q, int total_k, int max_seqlen_q, int D,
+                           int dtype, int causal, float scale, void* stream);
+
+/*
  * Backward of the prefill forward: dQ [B,H,N,D], dK, dV [B,Hkv,Nk,D] (dtype)
  * from Q, K, V, the forward's O and lse (natural-log logsumexp, fp32) and the
  * upstream gradient dO [B,H,N,D]; causal and scale as in the forward.  For
@@ -178,7 +196,8 @@ int b2a_decode_paged_noalloc(const void* q, const void* k_pool,
 /*
  * Device error word written by the kernels (bit 0: a bounded pipeline wait
  * timed out; bit 1: a paged-decode block-table entry was out of range;
- * bit 2: a KV append found no page for a position).  Reads and clears the
+ * bit 2: a KV append found no page for a position; bit 3: a varlen sequence
+ * was longer than max_seqlen_q or cu_seqlens was not non-decreasing).  Reads and clears the
  * word of the current device; this call synchronises the device.  *flags
  * receives the word.
  */

@@ -72,6 +72,36 @@ def naive_attention(Q, K, V, scale=None, causal=False, dtype=np.float64):
     return O, L
 
 
+def varlen_attention(Q, K, V, cu_q, cu_k, scale=None, causal=False, dtype=np.float64):
+    """Packed variable-length attention: Q [total_q,H,D], K/V [total_k,Hkv,D].
+
+    Sequence b is query tokens cu_q[b]..cu_q[b+1]-1 over keys
+    cu_k[b]..cu_k[b+1]-1, each computed as naive_attention of that one
+    sequence (the reference's per-(b, h) computation, ref/naive_attn.py:27-36).
+    Returns (O [total_q,H,D], L [H,total_q]).  Causal masks align per sequence
+    to its last key; a row that sees no key gets O = 0 and L = -inf.
+    """
+    Q = np.asarray(Q)
+    total_q, H, D = Q.shape
+    Hkv = K.shape[1]
+    scale = D ** -0.5 if scale is None else scale
+    O = np.zeros((total_q, H, D), dtype=dtype)
+    L = np.full((H, total_q), -np.inf, dtype=dtype)
+    for b in range(len(cu_q) - 1):
+        q0, q1, k0, k1 = int(cu_q[b]), int(cu_q[b + 1]), int(cu_k[b]), int(cu_k[b + 1])
+        n, nk = q1 - q0, k1 - k0
+        for h in range(H):
+            hk = _kv_head(h, H, Hkv)
+            for r in range(n):
+                last = (r + nk - n) if causal else nk - 1  # last visible key
+                if last < 0:
+                    continue
+                o, l = attention_head(Q[q0 + r, h][None], K[k0:k0 + last + 1, hk],
+                                      V[k0:k0 + last + 1, hk], scale, False, 0, dtype)
+                O[q0 + r, h], L[h, q0 + r] = o[0], l[0]
+    return O, L
+
+
 def attention_rows(Q, K, V, b, h, rows, scale=None, causal=False, dtype=np.float64):
     """O and L of selected query rows of head (b, h): for spot checks at large N."""
     B, H, N, D = Q.shape

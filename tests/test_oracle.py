@@ -148,3 +148,19 @@ def test_oracle_backward_matches_finite_differences():
         args2 = [a2 if arr is x else x for x in (q, k, v)]
         num = (f(*args1) - f(*args2)) / (2 * eps)
         np.testing.assert_allclose(grad[idx], num, rtol=1e-6, atol=1e-8)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_varlen_oracle_matches_dense(causal):
+    """Packed varlen with equal lengths is the dense computation re-laid out."""
+    B, H, Hkv, N, Nk, D = 2, 4, 2, 37, 53, 16
+    Q = ora.seeded_normal((B, H, N, D), 1)
+    K = ora.seeded_normal((B, Hkv, Nk, D), 2)
+    V = ora.seeded_normal((B, Hkv, Nk, D), 3)
+    O, L = ora.naive_attention(Q, K, V, causal=causal)
+    pk = lambda t: t.transpose(0, 2, 1, 3).reshape(-1, t.shape[1], D)
+    cu_q = np.arange(0, (B + 1) * N, N)
+    cu_k = np.arange(0, (B + 1) * Nk, Nk)
+    Ov, Lv = ora.varlen_attention(pk(Q), pk(K), pk(V), cu_q, cu_k, causal=causal)
+    np.testing.assert_allclose(Ov, pk(O), rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(Lv, L.transpose(1, 0, 2).reshape(H, -1), rtol=1e-12)
