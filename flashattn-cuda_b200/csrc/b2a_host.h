@@ -67,6 +67,8 @@ int decode_dispatch(const void* q, const void* k, const void* v, const int32_t* 
                     const int32_t* kv_lens, float* o_part, float* l_part, int B, int H, int Hkv,
                     int Lkv, int D, int splits, int tokens_per_split, int page_size, int max_pages,
                     int num_pages, int dtype, float scale, cudaStream_t stream);
+// fp32 workspace size of the backward (padded L/D rows + the dQ accumulator).
+int64_t backward_workspace_floats(int B, int H, int N, int D);
 int backward_dispatch(const void* q, const void* k, const void* v, const void* o, const void* dout,
                       const float* lse, void* dq, void* dk, void* dv, float* workspace, int B,
                       int H, int Hkv, int N, int Nk, int D, int dtype, int causal, float scale,

@@ -4,22 +4,36 @@
 // (cuda/flash_attn_kernel.cu:173-412): D_i = rowsum(dO * O), then dQ, then
 // dK / dV, recomputing P = exp(S - L) from the saved logsumexp.  Here:
 //
-//   * bwd_prep_kernel: D_i = rowsum(dO * O) in fp32 and a zeroed fp32 dQ
-//     accumulator (workspace);
-//   * bwd_main_kernel: one CTA per (64-key block j, KV head).  It keeps K_j,
-//     V_j in shared memory and dK_j, dV_j in registers, and walks every query
-//     head of the KV head (GQA group) and every 64-row query block i that sees
-//     block j (causal: from the diagonal on).  Per block:
-//         S^T = K_j Q_i^T            P^T = exp2(S^T scale log2e - L_i log2e)
-//         dV_j += P^T dO_i           dP^T = V_j dO_i^T
-//         dS^T = P^T (dP^T - D_i)    dK_j += dS^T Q_i
-//         dQ_i += dS K_j * scale  -> staged in shared memory, then ONE TMA bulk
-//                                     reduce-add of the 64 x D fp32 tile into
-//                                     the dQ accumulator (no per-element atomics)
-//     Q_i / dO_i arrive by TMA (128-byte swizzle) into a 2-stage ring fed by a
-//     producer warp; the products run on the tensor cores (mma.m16n8k16, each
-//     of the 4 consumer warps owning 16 of the 64 keys);
+//   * bwd_prep_kernel: per query row D_i = rowsum(dO * O) and L_i log2(e), in
+//     fp32 arrays padded to a multiple of 128 rows (padding rows: D = 0,
+//     L = +inf, so that their P is exactly 0), and a zeroed fp32 dQ
+//     accumulator;
+//   * bwd_main_kernel: one CTA per (128-key block j, KV head).  K_j, V_j stay
+//     in shared memory and dK_j, dV_j accumulate in TMEM while the CTA walks
+//     every query head of the KV head (GQA group) and every 128-row query
+//     block i that sees block j (causal: from the diagonal on).  Per step, on
+//     the 5th-generation tensor cores (tcgen05, M = 128):
+//         S^T  = K_j Q_i^T                      (SS UMMA -> TMEM)
+//         dP^T = V_j dO_i^T                     (SS UMMA -> TMEM)
+//         P^T  = exp2(S^T scale log2e - L_i log2e)     (element-wise warps,
+//         dS^T = P^T (dP^T - D_i)                       one key row per lane)
+//         dV_j += P^T dO_i                      (TS UMMA: P^T from TMEM)
+//         dK_j += dS^T Q_i                      (SS UMMA: dS^T from smem)
+//         dQ_i  = dS K_j                        (SS UMMA: the same dS^T tile
+//                                                read MN-major as A)
+//     and four read-out warps move dQ_i (TMEM -> registers -> a 128-byte
+//     swizzled staging tile) into the global fp32 dQ accumulator with TMA
+//     bulk reduce-adds (no per-element atomics);
 //   * bwd_dq_kernel: dQ accumulator (fp32, already scaled) -> dtype.
+//
+// Warp roles (512 threads): warps 0-7 element-wise (warp w owns TMEM lanes
+// 32 (w % 4) .. +31 = key rows, and query columns 64 (w / 4) .. +63); warps
+// 8-11 dQ read-out (lanes = query rows); warp 12 TMA producer; warp 13 UMMA
+// issuer and TMEM owner; warps 14-15 idle.
+//
+// TMEM (512 columns): S^T [0,128) with P^T written over it as packed 16-bit
+// pairs, dP^T [128,256) which the dQ product reuses once dP^T has been read,
+// dV [256, 256+D), dK [256+D, 256+2D).
 #include <cstdio>
 
 #include "sm100_ptx.cuh"
@@ -28,76 +42,76 @@
 namespace b2a {
 namespace bwd {
 
-constexpr int BQ = 64;  // query rows per step
-constexpr int BK = 64;  // keys per CTA (16 per consumer warp)
-constexpr int kConsumers = 4;
-constexpr int kThreads = (kConsumers + 1) * 32;
-constexpr int kProducerWarp = kConsumers;
-constexpr int kStages = 2;
-constexpr int kDsStride = BQ + 8;  // halves per row of the dS^T tile (pad: no bank conflicts)
+constexpr int BQ = 128;  // query rows per step (UMMA N of S^T, M of dQ)
+constexpr int BK = 128;  // keys per CTA (UMMA M of S^T, dV, dK)
+constexpr int kThreads = 512;
+constexpr int kReadoutWarp0 = 8;
+constexpr int kProducerWarp = 12;
+constexpr int kMmaWarp = 13;
+// Register split: launched at 128 per thread (512 threads), the element-wise
+// warpgroups take 176, the read-out warpgroup 104 and the control warpgroup 56:
+// 256 * 176 + 128 * 104 + 128 * 56 == 512 * 128.
+constexpr uint32_t kRegsElem = 176;
+constexpr uint32_t kRegsReadout = 104;
+constexpr uint32_t kRegsCtrl = 56;
+static_assert(256 * kRegsElem + 128 * kRegsReadout + 128 * kRegsCtrl == kThreads * 128,
+              "register split must add up to the launch allocation");
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 128, kColDV = 256;
+constexpr uint32_t kMaxSmem = 232448;  // 227 KB, the per-CTA limit
+constexpr uint32_t kErrSmemAlign = 16u;  // device error bit: base alignment slack too small
 
 template <int D>
 struct Cfg {
-  static constexpr int kBlocks = D / 64;
-  static constexpr uint32_t kTile = 64 * D * 2;  // one 64-row K, V, Q or dO tile
+  static constexpr int kBlocks = D / 64;            // 64-column (128-byte) blocks per row
+  static constexpr uint32_t kTile = 128 * D * 2;    // one 128-row K, V, Q or dO tile
+  static constexpr uint32_t kColDK = kColDV + D;
   static constexpr uint32_t kOffK = 0;
   static constexpr uint32_t kOffV = kOffK + kTile;
-  static constexpr uint32_t kOffQ = kOffV + kTile;                // [kStages]
-  static constexpr uint32_t kOffDO = kOffQ + kStages * kTile;     // [kStages]
-  static constexpr uint32_t kOffDQ = kOffDO + kStages * kTile;    // fp32 [2][BQ][D]
-  static constexpr uint32_t kOffDS = kOffDQ + 2 * BQ * D * 4;     // [BK][kDsStride]
-  static constexpr uint32_t kOffBar = kOffDS + BK * kDsStride * 2;
-  // kv_full, full[S], empty[S]
-  static constexpr int kNumBars = 1 + 2 * kStages;
-  static constexpr uint32_t kOffAbort = kOffBar + 8 * kNumBars;
-  static constexpr uint32_t kSmemBytes = kOffAbort + 16 + 1024;
+  static constexpr uint32_t kOffQ = kOffV + kTile;         // [2 stages]
+  static constexpr uint32_t kOffDO = kOffQ + 2 * kTile;    // [2 stages]
+  static constexpr uint32_t kOffDS = kOffDO + 2 * kTile;   // dS^T [128 keys][128 queries] 16-bit,
+                                                           // also the dQ staging tile
+  static constexpr uint32_t kOffVec = kOffDS + 128 * 128 * 2;  // [2 stages] {L2[128], D[128]}
+  static constexpr uint32_t kOffBar = kOffVec + 2 * 1024;
+  // kv_full, q_full[2], q_empty[2], s_full, dp_full, p_full, ds_full, dq_full,
+  // dq_free, ds_free, fin
+  static constexpr int kNumBars = 13;
+  static constexpr uint32_t kOffTmemSlot = kOffBar + 8 * kNumBars;
+  static constexpr uint32_t kOffAbort = kOffTmemSlot + 8;
+  static constexpr uint32_t kContent = kOffAbort + 8;
+  // + slack to align the base to 1024 bytes (128-byte swizzle atoms); the
+  // kernel checks at run time that the slack it needs fits
+  static constexpr uint32_t kSmemBytes =
+      kContent + 1024 <= kMaxSmem ? kContent + 1024 : kMaxSmem;
+  static_assert(kContent <= kMaxSmem, "backward tiles exceed shared memory");
 };
 
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t* r) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-template <bool BF16>
-__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  if constexpr (BF16)
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-  else
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// byte offset of element (row r, column c) of a 64-row tile written by TMA
-// with 128-byte swizzle in 64-column blocks
-__device__ __forceinline__ uint32_t sw_off(int r, int c) {
-  return (uint32_t)((c >> 6) * (64 * 128) + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) +
-                    (c & 7) * 2);
-}
-
-// D_i = rowsum(dO * O) (fp32) and a zeroed dQ accumulator; one warp per row.
+// Padded per-row arrays: L2 = L log2(e) (+inf past N) and D = rowsum(dO * O)
+// (0 past N), [B*H][Npad]; the valid rows of the dQ accumulator zeroed.  One
+// warp per padded row.
 template <int D, bool BF16>
 __global__ void bwd_prep_kernel(const void* __restrict__ o, const void* __restrict__ dout,
-                                float* __restrict__ dvec, float* __restrict__ dq_acc, int rows) {
+                                const float* __restrict__ lse, float* __restrict__ l2v,
+                                float* __restrict__ dvec, float* __restrict__ dq_acc, int N,
+                                int Npad, long long rows_pad) {
   using E = Elem<BF16>;
-  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const long long prow = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
+  if (prow >= rows_pad) return;
+  const long long bh = prow / Npad;
+  const int n = (int)(prow % Npad);
+  if (n >= N) {
+    if (lane == 0) {
+      dvec[prow] = 0.f;
+      l2v[prow] = INFINITY;
+    }
+    return;
+  }
+  const long long row = bh * N + n;
   constexpr int EPL = D / 32;  // elements per lane (2 or 4)
-  const typename E::T* op = reinterpret_cast<const typename E::T*>(o) + (size_t)row * D + lane * EPL;
-  const typename E::T* dp =
-      reinterpret_cast<const typename E::T*>(dout) + (size_t)row * D + lane * EPL;
+  const typename E::T* op = reinterpret_cast<const typename E::T*>(o) + row * D + lane * EPL;
+  const typename E::T* dp = reinterpret_cast<const typename E::T*>(dout) + row * D + lane * EPL;
   float acc = 0.f;
 #pragma unroll
   for (int e = 0; e < EPL; e += 2) {
@@ -107,8 +121,11 @@ __global__ void bwd_prep_kernel(const void* __restrict__ o, const void* __restri
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) dvec[row] = acc;
-  float* dqr = dq_acc + (size_t)row * D + lane * EPL;
+  if (lane == 0) {
+    dvec[prow] = acc;
+    l2v[prow] = lse[row] * 1.4426950408889634f;
+  }
+  float* dqr = dq_acc + row * D + lane * EPL;
 #pragma unroll
   for (int e = 0; e < EPL; ++e) dqr[e] = 0.f;
 }
@@ -124,275 +141,368 @@ __global__ void bwd_dq_kernel(const float* __restrict__ dq_acc, void* __restrict
   }
 }
 
+// byte offset of 16-byte chunk `chunk` (0..7) of row `row` inside a 128-byte
+// swizzled tile of 128-byte rows (the layout TMA and UMMA use)
+__device__ __forceinline__ uint32_t sw128(int row, int chunk) {
+  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// Bounded wait whose result is the same for every lane of the warp (a wait
+// that gave up on one lane stops the whole warp), so that the warp-collective
+// tcgen05 loads / stores and __syncwarp after it never see a split warp.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  const bool ok = mbar_wait(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+// The same over the 128 threads of the read-out warps (named barrier 3).
+__device__ __forceinline__ bool readout_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  const bool ok = mbar_wait(bar, parity, abort);
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred P, Q;\n\tsetp.ne.u32 P, %1, 0;\n\t"
+      "bar.red.and.pred Q, 3, 128, P;\n\tselp.u32 %0, 1, 0, Q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)ok)
+      : "memory");
+  return r != 0;
+}
+
 template <int D, bool BF16, bool CAUSAL>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_main_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmDO,
                     const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV,
-                    const __grid_constant__ CUtensorMap tmDQ, const float* __restrict__ lse,
+                    const __grid_constant__ CUtensorMap tmDQ, const float* __restrict__ l2v,
                     const float* __restrict__ dvec, void* __restrict__ dk, void* __restrict__ dv,
-                    int N, int Nk, int H, int Hkv, float scale) {
+                    int N, int Nk, int Npad, int H, int Hkv, float scale) {
   using C = Cfg<D>;
   using E = Elem<BF16>;
-  constexpr int S = kStages;
-  constexpr float kLog2e = 1.4426950408889634f;
-  const float scale_log2 = scale * kLog2e;
+  const float scale_log2 = scale * 1.4426950408889634f;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sb = (raw + 1023u) & ~1023u;
+  if ((sb - raw) + C::kContent > C::kSmemBytes) {  // uniform over the CTA
+    if (threadIdx.x == 0) atomicOr(&g_error_flags, kErrSmemAlign);
+    return;
+  }
   uint8_t* sp = smem_raw + (sb - raw);
   const uint32_t sK = sb + C::kOffK, sV = sb + C::kOffV;
   const uint32_t sQ = sb + C::kOffQ, sDO = sb + C::kOffDO;
-  const uint32_t sDQ = sb + C::kOffDQ, sDS = sb + C::kOffDS;
+  const uint32_t sDS = sb + C::kOffDS, sVec = sb + C::kOffVec;
   const uint32_t bar0 = sb + C::kOffBar;
   const uint32_t BAR_KV = bar0;
-  auto BAR_F = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto BAR_E = [&](int s) { return bar0 + 8u * (1 + S + s); };
+  auto BAR_QF = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto BAR_QE = [&](int s) { return bar0 + 8u * (3 + s); };
+  const uint32_t BAR_S = bar0 + 8u * 5, BAR_DP = bar0 + 8u * 6, BAR_P = bar0 + 8u * 7;
+  const uint32_t BAR_DS = bar0 + 8u * 8, BAR_DQ = bar0 + 8u * 9, BAR_DQF = bar0 + 8u * 10;
+  const uint32_t BAR_DSF = bar0 + 8u * 11, BAR_FIN = bar0 + 8u * 12;
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sp + C::kOffTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sp + C::kOffAbort);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = blockIdx.x;           // key block
-  const int bhk = blockIdx.y;         // b * Hkv + hkv
+  const int j = blockIdx.x;    // key block
+  const int bhk = blockIdx.y;  // b * Hkv + hkv
   const int b = bhk / Hkv, hkv = bhk % Hkv;
   const int G = H / Hkv;
   const int kv0 = j * BK;
   const int koff = Nk - N;  // causal: query row r sees keys <= r + koff
   const int nq = (N + BQ - 1) / BQ;
   const int i0 = CAUSAL ? max(0, (kv0 - koff) / BQ) : 0;
-  const int steps = G * max(0, nq - i0);  // (query head, query block) pairs
+  const int nqs = nq - i0;  // query blocks per query head (>= 1)
+  const int steps = G * nqs;  // (query head, query block) pairs
 
-  if (threadIdx.x == kProducerWarp * 32) {
+  if (warp == kProducerWarp && lane == 0) {
     mbar_init(BAR_KV, 1u);
-    for (int s = 0; s < S; ++s) {
-      mbar_init(BAR_F(s), 1u);
-      mbar_init(BAR_E(s), kConsumers);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(BAR_QF(s), 1u);
+      mbar_init(BAR_QE(s), 1u);
     }
+    mbar_init(BAR_S, 1u);
+    mbar_init(BAR_DP, 1u);
+    mbar_init(BAR_P, 8u);
+    mbar_init(BAR_DS, 8u);
+    mbar_init(BAR_DQ, 1u);
+    mbar_init(BAR_DQF, 4u);
+    mbar_init(BAR_DSF, 1u);
+    mbar_init(BAR_FIN, 1u);
     *abort_flag = 0;
     fence_mbar_init();
   }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32((const void*)tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
 
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------------ producer
-    if (lane == 0 && steps > 0) {
-      mbar_arrive_expect_tx(BAR_KV, 2 * C::kTile);
-#pragma unroll
-      for (int c = 0; c < C::kBlocks; ++c) {
-        tma_load_3d(sK + c * (64 * 128), &tmK, BAR_KV, c * 64, kv0, bhk);
-        tma_load_3d(sV + c * (64 * 128), &tmV, BAR_KV, c * 64, kv0, bhk);
-      }
-      for (int it = 0; it < steps; ++it) {
-        const int st = it % S;
-        if (it >= S && !mbar_wait(BAR_E(st), ((it / S) - 1) & 1, abort_flag)) break;
-        const int g = it / (nq - i0), qi = i0 + it % (nq - i0);
-        const int bh = b * H + hkv * G + g;
-        mbar_arrive_expect_tx(BAR_F(st), 2 * C::kTile);
+  if (warp >= kProducerWarp) {
+    setmaxnreg_dec<kRegsCtrl>();
+    if (warp == kProducerWarp) {
+      // ------------------------------------------------------------ producer
+      if (lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmDO);
+        mbar_arrive_expect_tx(BAR_KV, 2 * C::kTile);
 #pragma unroll
         for (int c = 0; c < C::kBlocks; ++c) {
-          tma_load_3d(sQ + st * C::kTile + c * (64 * 128), &tmQ, BAR_F(st), c * 64, qi * BQ, bh);
-          tma_load_3d(sDO + st * C::kTile + c * (64 * 128), &tmDO, BAR_F(st), c * 64, qi * BQ, bh);
+          tma_load_3d(sK + c * 16384, &tmK, BAR_KV, c * 64, kv0, bhk);
+          tma_load_3d(sV + c * 16384, &tmV, BAR_KV, c * 64, kv0, bhk);
+        }
+        for (int it = 0; it < steps; ++it) {
+          const int st = it & 1;
+          if (it >= 2 && !mbar_wait(BAR_QE(st), ((it >> 1) - 1) & 1, abort_flag)) break;
+          const int g = it / nqs, q0 = (i0 + it % nqs) * BQ;
+          const int bh = b * H + hkv * G + g;
+          mbar_arrive_expect_tx(BAR_QF(st), 2 * C::kTile + 1024);
+#pragma unroll
+          for (int c = 0; c < C::kBlocks; ++c) {
+            tma_load_3d(sQ + st * C::kTile + c * 16384, &tmQ, BAR_QF(st), c * 64, q0, bh);
+            tma_load_3d(sDO + st * C::kTile + c * 16384, &tmDO, BAR_QF(st), c * 64, q0, bh);
+          }
+          bulk_load(sVec + st * 1024, l2v + (size_t)bh * Npad + q0, 512, BAR_QF(st));
+          bulk_load(sVec + st * 1024 + 512, dvec + (size_t)bh * Npad + q0, 512, BAR_QF(st));
+        }
+      }
+    } else if (warp == kMmaWarp) {
+      // ------------------------------------------------------------ UMMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc_s = idesc_f16(128, 128, BF16, false, false);
+        constexpr uint32_t idesc_o = idesc_f16(128, D, BF16, false, true);
+        constexpr uint32_t idesc_q = idesc_f16(128, D, BF16, true, true);
+        bool ok = mbar_wait(BAR_KV, 0, abort_flag);
+        for (int it = 0; ok && it < steps; ++it) {
+          const int st = it & 1;
+          const uint32_t q_base = sQ + st * C::kTile, do_base = sDO + st * C::kTile;
+          if (!mbar_wait(BAR_QF(st), (it >> 1) & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          // S^T = K Q^T (A = K, B = Q, both K-major)
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_f16_ss(tmem + kColS, sdesc_sw128(sK + off, 16, 1024),
+                        sdesc_sw128(q_base + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(BAR_S);
+          // dP^T = V dO^T, into the columns dQ_{it-1} used: wait for its read-out
+          if (it > 0) {
+            if (!mbar_wait(BAR_DQF, (it - 1) & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_f16_ss(tmem + kColDP, sdesc_sw128(sV + off, 16, 1024),
+                        sdesc_sw128(do_base + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(BAR_DP);
+          // dV += P^T dO (A = P^T from TMEM: queries 64h.. packed from column
+          // 64h; B = dO MN-major: rows = queries = K, 64-column blocks of D = N)
+          if (!mbar_wait(BAR_P, it & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk)
+            umma_f16_ts(tmem + kColDV, tmem + kColS + (kk >> 2) * 64 + (kk & 3) * 8,
+                        sdesc_sw128(do_base + kk * 2048, 16384, 1024), idesc_o,
+                        (it > 0 || kk > 0) ? 1u : 0u);
+          // dK += dS^T Q (A = dS^T K-major: rows = keys, 64-query blocks;
+          // B = Q MN-major)
+          if (!mbar_wait(BAR_DS, it & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk)
+            umma_f16_ss(tmem + C::kColDK,
+                        sdesc_sw128(sDS + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                        sdesc_sw128(q_base + kk * 2048, 16384, 1024), idesc_o,
+                        (it > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(BAR_QE(st));  // Q_i / dO_i free once dV and dK have read them
+          // dQ = dS K (A = the dS^T tile read MN-major: rows = keys = K, columns
+          // = queries = M; B = K MN-major: rows = keys = K, columns = D = N)
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16_ss(tmem + kColDQ, sdesc_sw128(sDS + kk * 2048, 16384, 1024),
+                        sdesc_sw128(sK + kk * 2048, 16384, 1024), idesc_q, kk > 0 ? 1u : 0u);
+          umma_commit(BAR_DQ);
+        }
+        umma_commit(BAR_FIN);  // dK / dV final (or the pipeline gave up)
+      }
+    }
+  } else if (warp >= kReadoutWarp0) {
+    setmaxnreg_dec<kRegsReadout>();
+    // -------------------------------------------------------------- dQ read-out
+    const int row = (warp & 3) * 32 + lane;  // query row of the block = TMEM lane
+    const bool issuer = warp == kReadoutWarp0 && lane == 0;
+    for (int it = 0; it < steps; ++it) {
+      if (!readout_wait(BAR_DQ, it & 1, abort_flag)) break;
+      tc_fence_after();
+      const int g = it / nqs, q0 = (i0 + it % nqs) * BQ;
+      const int bh = b * H + hkv * G + g;
+#pragma unroll
+      for (int r = 0; r < D / 64; ++r) {
+        float v[64];
+        tmem_ld32(tmem + lane_base + kColDQ + r * 64, v);
+        tmem_ld32(tmem + lane_base + kColDQ + r * 64 + 32, v + 32);
+        tmem_ld_wait();
+        if (r == D / 64 - 1) {  // dQ fully in registers: its columns are free
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(BAR_DQF);
+        }
+        if (r > 0) {  // staging tile reused: wait until the last reduce read it
+          if (issuer) bulk_wait_group_read<0>();
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+        }
+        // two 32-column boxes, 128-byte swizzled: [box][row][8 chunks of 4 floats]
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const uint32_t addr = (uint32_t)((c >> 3) * 16384) + sw128(row, c & 7);
+          *reinterpret_cast<float4*>(sp + C::kOffDS + addr) =
+              make_float4(v[4 * c] * scale, v[4 * c + 1] * scale, v[4 * c + 2] * scale,
+                          v[4 * c + 3] * scale);
+        }
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (issuer) {
+          tma_reduce_add_3d(&tmDQ, sDS, r * 64, q0, bh);
+          tma_reduce_add_3d(&tmDQ, sDS + 16384, r * 64 + 32, q0, bh);
+          bulk_commit_group();
+        }
+      }
+      // the staging tile (= the dS^T tile) is free for the next step's dS^T
+      if (issuer) {
+        bulk_wait_group_read<0>();
+        mbar_arrive(BAR_DSF);
+      }
+    }
+    if (issuer) bulk_wait_group<0>();  // every dQ reduce has landed
+  } else {
+    setmaxnreg_inc<kRegsElem>();
+    // ------------------------------------------------------------ element-wise
+    const int krow = (warp & 3) * 32 + lane;  // key row of the block = TMEM lane
+    const int key = kv0 + krow;
+    const int h = warp >> 2;                  // query columns 64h .. 64h+63
+    bool ok = true;
+    for (int it = 0; it < steps; ++it) {
+      const int st = it & 1;
+      const int q0 = (i0 + it % nqs) * BQ;
+      const float* vec = reinterpret_cast<const float*>(sp + C::kOffVec + st * 1024);
+      const bool need_mask = (kv0 + BK > Nk) || (CAUSAL && kv0 + BK - 1 > q0 + koff);
+      // valid iff key <= q + koff: columns c >= qmin of this warp's 64
+      const int qmin = key - koff - (q0 + 64 * h);
+      // the L / D vectors arrived with Q_i (TMA): observe that barrier too
+      if (!warp_wait(BAR_QF(st), (it >> 1) & 1, abort_flag)) { ok = false; break; }
+      if (!warp_wait(BAR_S, it & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      float p[64];
+      tmem_ld32(tmem + lane_base + kColS + 64 * h, p);
+      tmem_ld32(tmem + lane_base + kColS + 64 * h + 32, p + 32);
+      tmem_ld_wait();
+      const float4* l2 = reinterpret_cast<const float4*>(vec + 64 * h);
+#pragma unroll
+      for (int c = 0; c < 64; c += 4) {
+        const float4 l = l2[c >> 2];
+        p[c] = ex2_mufu(fmaf(p[c], scale_log2, -l.x));
+        p[c + 1] = ex2_mufu(fmaf(p[c + 1], scale_log2, -l.y));
+        p[c + 2] = ex2_mufu(fmaf(p[c + 2], scale_log2, -l.z));
+        p[c + 3] = ex2_mufu(fmaf(p[c + 3], scale_log2, -l.w));
+      }
+      if (need_mask) {
+        const bool key_ok = key < Nk;
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (!key_ok || (CAUSAL && c < qmin)) p[c] = 0.f;
+      }
+      {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) pk[c] = pack2_u32<BF16>(p[2 * c], p[2 * c + 1]);
+        tmem_st32u(tmem + lane_base + kColS + 64 * h, pk);  // P^T over S^T
+        tmem_st_wait();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR_P);
+
+      if (!warp_wait(BAR_DP, it & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t ds[32];
+      const float4* dd = reinterpret_cast<const float4*>(vec + 128 + 64 * h);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float dp[32];
+        tmem_ld32(tmem + lane_base + kColDP + 64 * h + 32 * half, dp);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 32; c += 4) {
+          const float4 d4 = dd[(32 * half + c) >> 2];
+          const int pc = 32 * half + c;
+          ds[pc >> 1] = pack2_u32<BF16>(p[pc] * (dp[c] - d4.x), p[pc + 1] * (dp[c + 1] - d4.y));
+          ds[(pc >> 1) + 1] =
+              pack2_u32<BF16>(p[pc + 2] * (dp[c + 2] - d4.z), p[pc + 3] * (dp[c + 3] - d4.w));
+        }
+      }
+      // dP^T has been read (the dQ product may overwrite it after ds_full)
+      tc_fence_before();
+      if (it > 0 && !warp_wait(BAR_DSF, (it - 1) & 1, abort_flag)) { ok = false; break; }
+      // dS^T row -> block h of the tile, 8 chunks of 8 queries
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<uint4*>(sp + C::kOffDS + h * 16384 + sw128(krow, u)) =
+            make_uint4(ds[4 * u], ds[4 * u + 1], ds[4 * u + 2], ds[4 * u + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR_DS);
+    }
+
+    // ---- dV (warps 0-3) / dK (warps 4-7, scaled) of this key row
+    if (ok && warp_wait(BAR_FIN, 0, abort_flag)) {
+      tc_fence_after();
+      using T = typename E::T;
+      const uint32_t col = h ? C::kColDK : kColDV;
+      const float mul = h ? scale : 1.f;
+      T* out = reinterpret_cast<T*>(h ? dk : dv) + ((size_t)bhk * Nk + key) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem + lane_base + col + c * 32, v);
+        tmem_ld_wait();
+        if (key < Nk) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            w.x = pack2_u32<BF16>(v[i] * mul, v[i + 1] * mul);
+            w.y = pack2_u32<BF16>(v[i + 2] * mul, v[i + 3] * mul);
+            w.z = pack2_u32<BF16>(v[i + 4] * mul, v[i + 5] * mul);
+            w.w = pack2_u32<BF16>(v[i + 6] * mul, v[i + 7] * mul);
+            *reinterpret_cast<uint4*>(out + c * 32 + i) = w;
+          }
         }
       }
     }
-    return;
   }
 
-  // -------------------------------------------------------------------- consumers
-  const int g4 = lane >> 2, t4 = lane & 3;
-  const int r0 = warp * 16;  // this warp's first key row in the block
-  float dK[D / 8][4], dV[D / 8][4];
-#pragma unroll
-  for (int n = 0; n < D / 8; ++n)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) dK[n][e] = dV[n][e] = 0.f;
-  bool ok = steps == 0 || mbar_wait(BAR_KV, 0, abort_flag);
-
-  for (int it = 0; it < steps; ++it) {
-    const int st = it % S;
-    if (ok) ok = mbar_wait(BAR_F(st), (it / S) & 1, abort_flag);
-    // all consumer warps leave together if any wait gave up
-    {
-      uint32_t r;
-      asm volatile(
-          "{\n\t.reg .pred P, Q;\n\tsetp.ne.u32 P, %1, 0;\n\t"
-          "bar.red.and.pred Q, 1, 128, P;\n\tselp.u32 %0, 1, 0, Q;\n\t}"
-          : "=r"(r)
-          : "r"((uint32_t)ok)
-          : "memory");
-      if (!r) break;
-    }
-    const int g = it / (nq - i0), qi = i0 + it % (nq - i0);
-    const int bh = b * H + hkv * G + g;
-    const int q0 = qi * BQ;
-    const uint32_t q_base = sQ + st * C::kTile, do_base = sDO + st * C::kTile;
-
-    // per-column (query) constants of this lane: columns 8n + 2 t4 + {0, 1}
-    float l2[16], dd[16];
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int q = q0 + 8 * n + 2 * t4 + e;
-        const bool in = q < N;
-        l2[2 * n + e] = in ? lse[(size_t)bh * N + q] * kLog2e : INFINITY;
-        dd[2 * n + e] = in ? dvec[(size_t)bh * N + q] : 0.f;
-      }
-
-    // ---- S^T = K Q^T and dP^T = V dO^T (16 keys x 64 queries per warp)
-    float sT[8][4], dpT[8][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sT[n][e] = dpT[n][e] = 0.f;
-#pragma unroll
-    for (int kp = 0; kp < D / 32; ++kp) {  // two 16-column k-steps per pass
-      uint32_t ak0[4], ak1[4], av0[4], av1[4];
-      const int ar = r0 + (lane & 7) + 8 * ((lane >> 3) & 1);
-      const int ac = 32 * kp + 8 * (lane >> 4);
-      ldsm_x4(sK + sw_off(ar, ac), ak0);
-      ldsm_x4(sK + sw_off(ar, ac + 16), ak1);
-      ldsm_x4(sV + sw_off(ar, ac), av0);
-      ldsm_x4(sV + sw_off(ar, ac + 16), av1);
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        // B = Q^T / dO^T: query rows 8n..8n+7, columns 32kp + {0, 8, 16, 24}
-        uint32_t bq[4], bo[4];
-        const int br = 8 * n + (lane & 7), bc = 32 * kp + 8 * (lane >> 3);
-        ldsm_x4(q_base + sw_off(br, bc), bq);
-        ldsm_x4(do_base + sw_off(br, bc), bo);
-        mma16816<BF16>(sT[n], ak0, bq[0], bq[1]);
-        mma16816<BF16>(sT[n], ak1, bq[2], bq[3]);
-        mma16816<BF16>(dpT[n], av0, bo[0], bo[1]);
-        mma16816<BF16>(dpT[n], av1, bo[2], bo[3]);
-      }
-    }
-
-    // ---- P^T and dS^T = P^T (dP^T - D)
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = kv0 + r0 + g4 + 8 * (e >> 1);
-        const int q = q0 + 8 * n + 2 * t4 + (e & 1);
-        const bool valid = key < Nk && (!CAUSAL || key <= q + koff);
-        const float p = valid ? exp2f(fmaf(sT[n][e], scale_log2, -l2[2 * n + (e & 1)])) : 0.f;
-        sT[n][e] = p;
-        dpT[n][e] = p * (dpT[n][e] - dd[2 * n + (e & 1)]);
-      }
-
-    // ---- dV += P^T dO and dK += dS^T Q  (k = 64 queries, n = D)
-#pragma unroll
-    for (int kq = 0; kq < 4; ++kq) {
-      uint32_t ap[4], ads[4];
-      ap[0] = pack2_u32<BF16>(sT[2 * kq][0], sT[2 * kq][1]);
-      ap[1] = pack2_u32<BF16>(sT[2 * kq][2], sT[2 * kq][3]);
-      ap[2] = pack2_u32<BF16>(sT[2 * kq + 1][0], sT[2 * kq + 1][1]);
-      ap[3] = pack2_u32<BF16>(sT[2 * kq + 1][2], sT[2 * kq + 1][3]);
-      ads[0] = pack2_u32<BF16>(dpT[2 * kq][0], dpT[2 * kq][1]);
-      ads[1] = pack2_u32<BF16>(dpT[2 * kq][2], dpT[2 * kq][3]);
-      ads[2] = pack2_u32<BF16>(dpT[2 * kq + 1][0], dpT[2 * kq + 1][1]);
-      ads[3] = pack2_u32<BF16>(dpT[2 * kq + 1][2], dpT[2 * kq + 1][3]);
-      if (kq == 0) {
-        // dS^T of this warp's 16 keys -> shared memory (read back for dQ)
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          uint8_t* row_lo = sp + C::kOffDS + (size_t)(r0 + g4) * kDsStride * 2;
-          uint8_t* row_hi = row_lo + 8 * kDsStride * 2;
-          *reinterpret_cast<uint32_t*>(row_lo + (8 * n + 2 * t4) * 2) =
-              pack2_u32<BF16>(dpT[n][0], dpT[n][1]);
-          *reinterpret_cast<uint32_t*>(row_hi + (8 * n + 2 * t4) * 2) =
-              pack2_u32<BF16>(dpT[n][2], dpT[n][3]);
-        }
-      }
-#pragma unroll
-      for (int nd = 0; nd < D / 8; nd += 2) {
-        // B = dO / Q rows 16kq.. (k), columns 8nd.. (n): transposed loads
-        const int br = 16 * kq + (lane & 7) + 8 * ((lane >> 3) & 1), bc = 8 * nd + 8 * (lane >> 4);
-        uint32_t bo[4], bq[4];
-        ldsm_x4_t(do_base + sw_off(br, bc), bo);
-        ldsm_x4_t(q_base + sw_off(br, bc), bq);
-        mma16816<BF16>(dV[nd], ap, bo[0], bo[1]);
-        mma16816<BF16>(dV[nd + 1], ap, bo[2], bo[3]);
-        mma16816<BF16>(dK[nd], ads, bq[0], bq[1]);
-        mma16816<BF16>(dK[nd + 1], ads, bq[2], bq[3]);
-      }
-    }
-
-    // ---- dQ_i += dS K * scale (this warp: queries 16w..16w+15, all D columns)
-    asm volatile("bar.sync 1, 128;" ::: "memory");  // dS^T tile complete
-    const uint32_t dq_buf = sDQ + (it & 1) * (BQ * D * 4);
-    if (it >= 2 && warp == 0 && lane == 0) bulk_wait_group_read<1>();  // buffer reused
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    {
-      float acc[D / 8][4];
-#pragma unroll
-      for (int n = 0; n < D / 8; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < BK / 16; ++kk) {
-        // A = dS (m = queries, k = keys) from the dS^T tile [keys][queries]
-        uint32_t a[4];
-        const int ar = 16 * kk + (lane & 7) + 8 * (lane >> 4), ac = 16 * warp + 8 * ((lane >> 3) & 1);
-        // blocks (k 0-7, m 0-7), (k 0-7, m 8-15), (k 8-15, m 0-7), (k 8-15, m 8-15)
-        // transposed: exactly the A fragment a0..a3
-        ldsm_x4_t(sDS + (uint32_t)(ar * kDsStride + ac) * 2, a);
-        const uint32_t* af = a;
-#pragma unroll
-        for (int nd = 0; nd < D / 8; nd += 2) {
-          const int br = 16 * kk + (lane & 7) + 8 * ((lane >> 3) & 1), bc = 8 * nd + 8 * (lane >> 4);
-          uint32_t bk[4];
-          ldsm_x4_t(sK + sw_off(br, bc), bk);
-          mma16816<BF16>(acc[nd], af, bk[0], bk[1]);
-          mma16816<BF16>(acc[nd + 1], af, bk[2], bk[3]);
-        }
-      }
-      // stage the scaled fp32 tile (row-major [BQ][D]) for the bulk reduce
-      float* dqs = reinterpret_cast<float*>(sp + (dq_buf - sb));
-#pragma unroll
-      for (int n = 0; n < D / 8; ++n) {
-        const int row = 16 * warp + g4, col = 8 * n + 2 * t4;
-        *reinterpret_cast<float2*>(dqs + row * D + col) =
-            make_float2(acc[n][0] * scale, acc[n][1] * scale);
-        *reinterpret_cast<float2*>(dqs + (row + 8) * D + col) =
-            make_float2(acc[n][2] * scale, acc[n][3] * scale);
-      }
-    }
-    fence_proxy_async_smem();
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (warp == 0 && lane == 0) {
-      tma_reduce_add_3d(&tmDQ, dq_buf, 0, q0, bh);
-      bulk_commit_group();
-    }
-    // release Q_i / dO_i
-    __syncwarp();
-    if (lane == 0) mbar_arrive(BAR_E(st));
-  }
-  if (warp == 0 && lane == 0) bulk_wait_group<0>();  // every dQ reduce has landed
-
-  // ---- dK (scaled), dV of this warp's 16 keys
-  if (ok) {
-    using T = typename E::T;
-#pragma unroll
-    for (int n = 0; n < D / 8; ++n)
-#pragma unroll
-      for (int hi = 0; hi < 2; ++hi) {
-        const int key = kv0 + r0 + g4 + 8 * hi;
-        if (key >= Nk) continue;
-        const size_t off = ((size_t)bhk * Nk + key) * D + 8 * n + 2 * t4;
-        *reinterpret_cast<typename E::T2*>(reinterpret_cast<T*>(dk) + off) =
-            E::pack(dK[n][2 * hi] * scale, dK[n][2 * hi + 1] * scale);
-        *reinterpret_cast<typename E::T2*>(reinterpret_cast<T*>(dv) + off) =
-            E::pack(dV[n][2 * hi], dV[n][2 * hi + 1]);
-      }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
 }  // namespace bwd
 
 B2A_DEFINE_ERROR_READER(backward)
+
+// Workspace (fp32): L2 [B*H][Npad], D [B*H][Npad], dQ accumulator [B*H*N*D];
+// Npad = N rounded up to 128 (every region starts 512-byte aligned).
+int64_t backward_workspace_floats(int B, int H, int N, int D) {
+  const int64_t npad = ((int64_t)N + bwd::BQ - 1) / bwd::BQ * bwd::BQ;
+  return 2 * (int64_t)B * H * npad + (int64_t)B * H * N * D;
+}
 
 template <int D, bool BF16, bool CAUSAL>
 static int launch_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
@@ -411,11 +521,13 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
     if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(backward)");
     attr_done[dev] = true;
   }
-  const size_t rows = (size_t)B * H * N;
-  float* dvec = ws;                 // [B*H*N]
-  float* dq_acc = ws + ((rows + 63) / 64) * 64;  // [B*H*N*D], 256-byte aligned
-  bwd_prep_kernel<D, BF16><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(o, dout, dvec, dq_acc,
-                                                                           (int)rows);
+  const int npad = (N + BQ - 1) / BQ * BQ;
+  const long long rows_pad = (long long)B * H * npad;
+  float* l2v = ws;
+  float* dvec = ws + rows_pad;
+  float* dq_acc = ws + 2 * rows_pad;
+  bwd_prep_kernel<D, BF16><<<(unsigned)((rows_pad + 7) / 8), 256, 0, stream>>>(
+      o, dout, lse, l2v, dvec, dq_acc, N, npad, rows_pad);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "backward prep launch");
   const CUtensorMapDataType dt =
@@ -425,16 +537,16 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
   if (rc == B2A_OK) rc = make_tmap_3d(&tdo, dout, dt, D, N, (uint64_t)B * H, 64, BQ, true);
   if (rc == B2A_OK) rc = make_tmap_3d(&tk, k, dt, D, Nk, (uint64_t)B * Hkv, 64, BK, true);
   if (rc == B2A_OK) rc = make_tmap_3d(&tv, v, dt, D, Nk, (uint64_t)B * Hkv, 64, BK, true);
-  if (rc == B2A_OK)
-    rc = make_tmap_3d(&tdq, dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, D, N, (uint64_t)B * H, D, BQ,
-                      false, 4);
+  if (rc == B2A_OK)  // 32 fp32 = 128-byte boxes, swizzled like the staging tile
+    rc = make_tmap_3d(&tdq, dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, D, N, (uint64_t)B * H, 32,
+                      BQ, true, 4);
   if (rc != B2A_OK) return rc;
   dim3 grid((unsigned)((Nk + BK - 1) / BK), (unsigned)(B * Hkv));
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tq, tdo, tk, tv, tdq, lse, dvec, dk, dv, N, Nk,
-                                                   H, Hkv, scale);
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tq, tdo, tk, tv, tdq, l2v, dvec, dk, dv, N, Nk,
+                                                   npad, H, Hkv, scale);
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "backward kernel launch");
-  const size_t n = rows * D;
+  const size_t n = (size_t)B * H * N * D;
   bwd_dq_kernel<D, BF16><<<(unsigned)((n / 2 + 255) / 256), 256, 0, stream>>>(dq_acc, dq, n);
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "backward dQ launch");

@@ -342,8 +342,7 @@ int b2a_backward(const void* q, const void* k, const void* v, const void* o, con
 }
 
 int64_t b2a_backward_workspace_floats(int B, int H, int N, int D) {
-  const int64_t rows = (int64_t)B * H * N;
-  return ((rows + 63) / 64) * 64 + rows * D;
+  return backward_workspace_floats(B, H, N, D);
 }
 
 int b2a_kv_append_paged(const void* k_new, const void* v_new, void* k_pool, void* v_pool,

@@ -197,7 +197,9 @@ int b2a_decode_paged_noalloc(const void* q, const void* k_pool,
  * Device error word written by the kernels (bit 0: a bounded pipeline wait
  * timed out; bit 1: a paged-decode block-table entry was out of range;
  * bit 2: a KV append found no page for a position; bit 3: a varlen sequence
- * was longer than max_seqlen_q or cu_seqlens was not non-decreasing).  Reads and clears the
+ * was longer than max_seqlen_q or cu_seqlens was not non-decreasing; bit 4:
+ * the backward kernel found too little shared memory to align its tiles and
+ * did nothing).  Reads and clears the
  * word of the current device; this call synchronises the device.  *flags
  * receives the word.
  */
