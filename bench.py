@@ -62,6 +62,14 @@ CONFIGS = {
     "5a": dict(kind="paged", B=128, H=32, Hkv=8, D=128, page=16, lmin=512, lmax=32768,
                dtype="float16", pps=64, shard=True,
                name="config5a: paged decode B=128 H=32 Hkv=8 D=128 fp16 page=16 len U[512,32768]"),
+    # training counterparts: the backward (dQ, dK, dV) at the config 3 / config 2 shapes
+    "7": dict(kind="backward", B=4, H=32, Hkv=32, N=8192, D=128, dtype="bfloat16", causal=True,
+              shard=True, name="backward B=4 H=32 N=8192 D=128 bf16 causal (config 3 shape)"),
+    "7s": dict(kind="backward", B=1, H=8, Hkv=8, N=4096, D=64, dtype="float16", causal=False,
+               shard=False, name="backward B=1 H=8 N=4096 D=64 fp16 (config 2 shape)"),
+    # config 7 at 1/16 of the heads (128 MB of inputs and gradients): the case ncu captures run on
+    "7m": dict(kind="backward", B=1, H=8, Hkv=8, N=8192, D=128, dtype="bfloat16", causal=True,
+               shard=True, name="backward B=1 H=8 N=8192 D=128 bf16 causal (config 7, small)"),
     "6": dict(kind="varlen", B=16, H=32, Hkv=8, D=128, lmin=256, lmax=8192, dtype="bfloat16",
               causal=True, shard=True,
               name="varlen prefill fwd: 16 packed sequences len U[256,8192] H=32 Hkv=8 D=128 "
@@ -173,6 +181,18 @@ def cpu_sample(cfg_key: str, steps: int, warmup: int):
     from oracle import attention as ora
     c = CONFIGS[cfg_key]
     cores = os.cpu_count() or 1
+    if c["kind"] == "backward":
+        # one (b, h) head at a bounded length per step
+        N, D = min(c["N"], 2048), c["D"]
+        q, k, v, do = (ora.seeded_normal((1, 1, N, D), s) for s in (1, 2, 3, 4))
+        for i in range(warmup + steps):
+            if i == warmup:
+                start = time.perf_counter()
+            ora.attention_backward(q, k, v, do, None, c["causal"], np.float32)
+        el = time.perf_counter() - start
+        flops = 10 * D * N * N * (0.5 if c["causal"] else 1.0) * steps
+        return flops / el / 1e12, "TFLOP/s", \
+            f"one (b,h) head, N={N}, fp32 numpy naive backward, per step", cores
     if c["kind"] in ("prefill", "varlen"):
         # one (b, h) head per step (rows limited for the causal N=8192 case);
         # varlen: one head of a sequence of the median length
@@ -265,6 +285,48 @@ def run_ours(args, rank, world, local_rank):
 
         workload = dict(workload=c["name"], B=Bl, H=Hl, N=c["N"], D=c["D"],
                         causal=c["causal"], dtype=c["dtype"], units_per_rank=Bl * Hl)
+    elif c["kind"] == "backward":
+        units = c["B"] * c["H"]
+        if c["shard"]:
+            assert units % world == 0
+            units //= world
+            Bl, Hl = (1, units) if units < c["H"] else (units // c["H"], c["H"])
+        else:
+            Bl, Hl = c["B"], c["H"]
+        shape = (Bl, Hl, c["N"], c["D"])
+        set_bytes = 8 * np.prod(shape) * 2  # q k v O dO + dq dk dv
+        nsets = max(1, int(np.ceil(1.5 * L2_BYTES / set_bytes))) if set_bytes < L2_BYTES else 1
+        sets = []
+        for _ in range(nsets):
+            q, k, v, do = (torch.randn(shape, device=dev, generator=gen).to(tdt) for _ in range(4))
+            O, L = b200attn.forward(q, k, v, causal=c["causal"])
+            sets.append((q, k, v, O, do, L))
+        # 5 products of 2*N*N*D FLOPs each (S, dP, dV, dK, dQ); causal: the unmasked half
+        work_per_step = 10 * c["N"] * c["N"] * c["D"] * Bl * Hl * (0.5 if c["causal"] else 1.0)
+        unit = "TFLOP/s"
+
+        def step(i):
+            return b200attn.backward(*sets[i % nsets], causal=c["causal"])
+
+        kernel_regex = "bwd_main_kernel"
+        bound, peak = "tensor", None
+        n_el = int(np.prod(shape))
+        h2d = 5 * n_el * 2 + int(np.prod(shape[:3])) * 4
+        d2h = 3 * n_el * 2
+        hg = torch.Generator().manual_seed(rank)
+        host_in = [torch.randn(shape, generator=hg).to(tdt).pin_memory() for _ in range(5)]
+        host_in.append(torch.randn(shape[:3], generator=hg).abs().pin_memory())
+        host_out = tuple(torch.empty(shape, dtype=tdt).pin_memory() for _ in range(3))
+
+        e2e_in = host_in
+        static_out = False
+
+        def e2e_run(q, k, v, O, do, L):
+            return b200attn.backward(q, k, v, O, do, L, causal=c["causal"])
+
+        workload = dict(workload=c["name"], B=Bl, H=Hl, N=c["N"], D=c["D"], causal=c["causal"],
+                        dtype=c["dtype"], units_per_rank=Bl * Hl,
+                        flops="10*N^2*D per (b,h) (x0.5 causal): S, dP, dV, dK, dQ")
     elif c["kind"] == "varlen":
         lens_all = varlen_lengths(c)
         # greedy balance of sequences over ranks by attention work (~ n^2)
@@ -579,7 +641,8 @@ def run_ours(args, rank, world, local_rank):
             v, u, sample, cores = cpu_sample(args.config, steps=2, warmup=1)
             cpu = {"value": round(v, 6), "unit": u, "cores": cores, "kind": "port",
                    "sample": sample}
-        kernel_launches = args.steps * (1 if c["kind"] in ("prefill", "varlen") else 2)  # timed region only
+        per_step = {"prefill": 1, "varlen": 1, "backward": 3}.get(c["kind"], 2)
+        kernel_launches = args.steps * per_step  # timed region only
         out = {
             "metric": METRIC,
             "value": round(value, 3),

@@ -10,30 +10,33 @@
 //     accumulator;
 //   * bwd_main_kernel: one CTA per (128-key block j, KV head).  K_j, V_j stay
 //     in shared memory and dK_j, dV_j accumulate in TMEM while the CTA walks
-//     every query head of the KV head (GQA group) and every 128-row query
-//     block i that sees block j (causal: from the diagonal on).  Per step, on
-//     the 5th-generation tensor cores (tcgen05, M = 128):
+//     every query head of the KV head (GQA group) and every query block i of
+//     BQ rows that sees block j (causal: from the diagonal on).  BQ = 128 for
+//     D = 64 and 64 for D = 128.  Per step, on the 5th-generation tensor cores
+//     (tcgen05, cta_group::1):
 //         S^T  = K_j Q_i^T                      (SS UMMA -> TMEM)
 //         dP^T = V_j dO_i^T                     (SS UMMA -> TMEM)
 //         P^T  = exp2(S^T scale log2e - L_i log2e)     (element-wise warps,
 //         dS^T = P^T (dP^T - D_i)                       one key row per lane)
 //         dV_j += P^T dO_i                      (TS UMMA: P^T from TMEM)
 //         dK_j += dS^T Q_i                      (SS UMMA: dS^T from smem)
-//         dQ_i  = dS K_j                        (SS UMMA: the same dS^T tile
-//                                                read MN-major as A)
+//         dQ_i  = dS K_j        (D = 64)        (SS UMMA: the dS^T tile read
+//         dQ_i^T = K_j^T dS^T   (D = 128)        MN-major; M = 128 either way)
 //     and four read-out warps move dQ_i (TMEM -> registers -> a 128-byte
-//     swizzled staging tile) into the global fp32 dQ accumulator with TMA
-//     bulk reduce-adds (no per-element atomics);
+//     swizzled fp32 staging tile) into the global fp32 dQ accumulator with
+//     TMA bulk reduce-adds (no per-element atomics).  The dS^T tiles and the
+//     staging tiles are double-buffered, so a step never waits for the
+//     previous step's reduce to finish reading;
 //   * bwd_dq_kernel: dQ accumulator (fp32, already scaled) -> dtype.
 //
 // Warp roles (512 threads): warps 0-7 element-wise (warp w owns TMEM lanes
-// 32 (w % 4) .. +31 = key rows, and query columns 64 (w / 4) .. +63); warps
-// 8-11 dQ read-out (lanes = query rows); warp 12 TMA producer; warp 13 UMMA
-// issuer and TMEM owner; warps 14-15 idle.
+// 32 (w % 4) .. +31 = key rows, and query columns W (w / 4) .. +W-1, W =
+// BQ / 2); warps 8-11 dQ read-out; warp 12 TMA producer; warp 13 UMMA issuer
+// and TMEM owner; warps 14-15 idle.
 //
-// TMEM (512 columns): S^T [0,128) with P^T written over it as packed 16-bit
-// pairs, dP^T [128,256) which the dQ product reuses once dP^T has been read,
-// dV [256, 256+D), dK [256+D, 256+2D).
+// TMEM columns: S^T [0,BQ) with P^T written over it as packed 16-bit pairs,
+// dP^T [BQ,2BQ), dV [2BQ, 2BQ+D), dK [2BQ+D, 2BQ+2D), dQ (or dQ^T) from
+// 2BQ+2D: 448 of 512 columns for both head dimensions.
 #include <cstdio>
 
 #include "sm100_ptx.cuh"
@@ -42,7 +45,6 @@
 namespace b2a {
 namespace bwd {
 
-constexpr int BQ = 128;  // query rows per step (UMMA N of S^T, M of dQ)
 constexpr int BK = 128;  // keys per CTA (UMMA M of S^T, dV, dK)
 constexpr int kThreads = 512;
 constexpr int kReadoutWarp0 = 8;
@@ -57,26 +59,53 @@ constexpr uint32_t kRegsCtrl = 56;
 static_assert(256 * kRegsElem + 128 * kRegsReadout + 128 * kRegsCtrl == kThreads * 128,
               "register split must add up to the launch allocation");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 128, kColDV = 256;
-constexpr uint32_t kMaxSmem = 232448;  // 227 KB, the per-CTA limit
+constexpr uint32_t kMaxSmem = 232448;    // 227 KB, the per-CTA limit
 constexpr uint32_t kErrSmemAlign = 16u;  // device error bit: base alignment slack too small
+constexpr int kPadRows = 128;            // L2 / D rows are padded to a multiple of this
+// of every 4 consecutive (even, odd) score pairs, this many take the
+// polynomial exp2 on the FMA pipe and the rest the MUFU ex2 (16 per clock
+// per SM): half and half keeps both pipes equally busy
+constexpr int kPolyPairsPer4 = 2;
+constexpr int BQ = 128;  // query rows per step (UMMA N of S^T, M of dQ)
 
+// Shared-memory plan per head dimension (both under 227 KB):
+//   D = 64:  Q and dO share a 2-stage ring; 2 dS^T tiles; 2 fp32 staging
+//            tiles; dQ has its own TMEM columns.
+//   D = 128: Q in a 2-stage ring, dO single-buffered (reloaded as soon as dV
+//            has read it); 1 dS^T tile; one 32 KB staging tile that the dQ
+//            read-out fills in two 64-column rounds; dQ reuses the dP^T
+//            columns (TMEM is full: S^T, dP^T, dV, dK = 4 x 128).
 template <int D>
 struct Cfg {
+  static constexpr bool kWide = (D == 128);
+  static constexpr int W = BQ / 2;                  // query columns per element-wise warp
   static constexpr int kBlocks = D / 64;            // 64-column (128-byte) blocks per row
-  static constexpr uint32_t kTile = 128 * D * 2;    // one 128-row K, V, Q or dO tile
-  static constexpr uint32_t kColDK = kColDV + D;
+  static constexpr int kDoStages = kWide ? 1 : 2;
+  static constexpr int kDsBufs = kWide ? 1 : 2;
+  static constexpr int kStBufs = kWide ? 1 : 2;     // staging tiles of BQ x 64 fp32
+  static constexpr int kRounds = D / 64;            // staging rounds per step
+  static constexpr uint32_t kTile = 128 * D * 2;    // K, V, Q or dO tile (128 rows)
+  static constexpr uint32_t kBlk = 128 * 128;       // one 64-column block of a tile
+  static constexpr uint32_t kDsTile = BK * BQ * 2;  // dS^T [128 keys][128 queries]
+  static constexpr uint32_t kStBox = BQ * 128;      // staging box: BQ rows x 32 fp32
+  static constexpr uint32_t kStTile = 2 * kStBox;   // 64 fp32 columns
+  static constexpr uint32_t kVec = BQ * 8;          // {L2[BQ], D[BQ]}
+  // TMEM columns
+  static constexpr uint32_t kColS = 0, kColDP = BQ, kColDV = 2 * BQ, kColDK = 2 * BQ + D;
+  static constexpr uint32_t kColDQ = kWide ? kColDP : 2 * BQ + 2 * D;
+  static_assert((kWide ? kColDK + D : kColDQ + D) <= kTmemCols, "TMEM layout");
+  // shared memory
   static constexpr uint32_t kOffK = 0;
   static constexpr uint32_t kOffV = kOffK + kTile;
-  static constexpr uint32_t kOffQ = kOffV + kTile;         // [2 stages]
-  static constexpr uint32_t kOffDO = kOffQ + 2 * kTile;    // [2 stages]
-  static constexpr uint32_t kOffDS = kOffDO + 2 * kTile;   // dS^T [128 keys][128 queries] 16-bit,
-                                                           // also the dQ staging tile
-  static constexpr uint32_t kOffVec = kOffDS + 128 * 128 * 2;  // [2 stages] {L2[128], D[128]}
-  static constexpr uint32_t kOffBar = kOffVec + 2 * 1024;
+  static constexpr uint32_t kOffQ = kOffV + kTile;                 // [2 stages]
+  static constexpr uint32_t kOffDO = kOffQ + 2 * kTile;            // [kDoStages]
+  static constexpr uint32_t kOffDS = kOffDO + kDoStages * kTile;   // [kDsBufs]
+  static constexpr uint32_t kOffST = kOffDS + kDsBufs * kDsTile;   // [kStBufs]
+  static constexpr uint32_t kOffVec = kOffST + kStBufs * kStTile;  // [2 stages]
+  static constexpr uint32_t kOffBar = kOffVec + 2 * kVec;
   // kv_full, q_full[2], q_empty[2], s_full, dp_full, p_full, ds_full, dq_full,
-  // dq_free, ds_free, fin
-  static constexpr int kNumBars = 13;
+  // dq_free, ds_empty[2], do_full, do_empty, fin
+  static constexpr int kNumBars = 16;
   static constexpr uint32_t kOffTmemSlot = kOffBar + 8 * kNumBars;
   static constexpr uint32_t kOffAbort = kOffTmemSlot + 8;
   static constexpr uint32_t kContent = kOffAbort + 8;
@@ -178,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     int N, int Nk, int Npad, int H, int Hkv, float scale) {
   using C = Cfg<D>;
   using E = Elem<BF16>;
+  constexpr int W = C::W;
   const float scale_log2 = scale * 1.4426950408889634f;
 
   extern __shared__ uint8_t smem_raw[];
@@ -190,14 +220,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sp = smem_raw + (sb - raw);
   const uint32_t sK = sb + C::kOffK, sV = sb + C::kOffV;
   const uint32_t sQ = sb + C::kOffQ, sDO = sb + C::kOffDO;
-  const uint32_t sDS = sb + C::kOffDS, sVec = sb + C::kOffVec;
+  const uint32_t sDS = sb + C::kOffDS, sST = sb + C::kOffST, sVec = sb + C::kOffVec;
   const uint32_t bar0 = sb + C::kOffBar;
   const uint32_t BAR_KV = bar0;
   auto BAR_QF = [&](int s) { return bar0 + 8u * (1 + s); };
   auto BAR_QE = [&](int s) { return bar0 + 8u * (3 + s); };
   const uint32_t BAR_S = bar0 + 8u * 5, BAR_DP = bar0 + 8u * 6, BAR_P = bar0 + 8u * 7;
   const uint32_t BAR_DS = bar0 + 8u * 8, BAR_DQ = bar0 + 8u * 9, BAR_DQF = bar0 + 8u * 10;
-  const uint32_t BAR_DSF = bar0 + 8u * 11, BAR_FIN = bar0 + 8u * 12;
+  auto BAR_DSE = [&](int s) { return bar0 + 8u * (11 + s); };
+  const uint32_t BAR_DOF = bar0 + 8u * 13, BAR_DOE = bar0 + 8u * 14;  // single-buffered dO
+  const uint32_t BAR_FIN = bar0 + 8u * 15;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sp + C::kOffTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sp + C::kOffAbort);
 
@@ -210,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int koff = Nk - N;  // causal: query row r sees keys <= r + koff
   const int nq = (N + BQ - 1) / BQ;
   const int i0 = CAUSAL ? max(0, (kv0 - koff) / BQ) : 0;
-  const int nqs = nq - i0;  // query blocks per query head (>= 1)
+  const int nqs = nq - i0;    // query blocks per query head (>= 1)
   const int steps = G * nqs;  // (query head, query block) pairs
 
   if (warp == kProducerWarp && lane == 0) {
@@ -218,6 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(BAR_QF(s), 1u);
       mbar_init(BAR_QE(s), 1u);
+      mbar_init(BAR_DSE(s), 1u);
     }
     mbar_init(BAR_S, 1u);
     mbar_init(BAR_DP, 1u);
@@ -225,7 +258,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(BAR_DS, 8u);
     mbar_init(BAR_DQ, 1u);
     mbar_init(BAR_DQF, 4u);
-    mbar_init(BAR_DSF, 1u);
+    mbar_init(BAR_DOF, 1u);
+    mbar_init(BAR_DOE, 1u);
     mbar_init(BAR_FIN, 1u);
     *abort_flag = 0;
     fence_mbar_init();
@@ -250,65 +284,82 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(BAR_KV, 2 * C::kTile);
 #pragma unroll
         for (int c = 0; c < C::kBlocks; ++c) {
-          tma_load_3d(sK + c * 16384, &tmK, BAR_KV, c * 64, kv0, bhk);
-          tma_load_3d(sV + c * 16384, &tmV, BAR_KV, c * 64, kv0, bhk);
+          tma_load_3d(sK + c * C::kBlk, &tmK, BAR_KV, c * 64, kv0, bhk);
+          tma_load_3d(sV + c * C::kBlk, &tmV, BAR_KV, c * 64, kv0, bhk);
         }
         for (int it = 0; it < steps; ++it) {
           const int st = it & 1;
-          if (it >= 2 && !mbar_wait(BAR_QE(st), ((it >> 1) - 1) & 1, abort_flag)) break;
           const int g = it / nqs, q0 = (i0 + it % nqs) * BQ;
           const int bh = b * H + hkv * G + g;
-          mbar_arrive_expect_tx(BAR_QF(st), 2 * C::kTile + 1024);
+          if (it >= 2 && !mbar_wait(BAR_QE(st), ((it >> 1) - 1) & 1, abort_flag)) break;
+          constexpr bool kDoInRing = C::kDoStages == 2;
+          mbar_arrive_expect_tx(BAR_QF(st), (kDoInRing ? 2 : 1) * C::kTile + C::kVec);
 #pragma unroll
           for (int c = 0; c < C::kBlocks; ++c) {
-            tma_load_3d(sQ + st * C::kTile + c * 16384, &tmQ, BAR_QF(st), c * 64, q0, bh);
-            tma_load_3d(sDO + st * C::kTile + c * 16384, &tmDO, BAR_QF(st), c * 64, q0, bh);
+            tma_load_3d(sQ + st * C::kTile + c * C::kBlk, &tmQ, BAR_QF(st), c * 64, q0, bh);
+            if (kDoInRing)
+              tma_load_3d(sDO + st * C::kTile + c * C::kBlk, &tmDO, BAR_QF(st), c * 64, q0, bh);
           }
-          bulk_load(sVec + st * 1024, l2v + (size_t)bh * Npad + q0, 512, BAR_QF(st));
-          bulk_load(sVec + st * 1024 + 512, dvec + (size_t)bh * Npad + q0, 512, BAR_QF(st));
+          bulk_load(sVec + st * C::kVec, l2v + (size_t)bh * Npad + q0, BQ * 4, BAR_QF(st));
+          bulk_load(sVec + st * C::kVec + BQ * 4, dvec + (size_t)bh * Npad + q0, BQ * 4,
+                    BAR_QF(st));
+          if (!kDoInRing) {  // dO_it once dV_{it-1} has read dO_{it-1}
+            if (it >= 1 && !mbar_wait(BAR_DOE, (it - 1) & 1, abort_flag)) break;
+            mbar_arrive_expect_tx(BAR_DOF, C::kTile);
+#pragma unroll
+            for (int c = 0; c < C::kBlocks; ++c)
+              tma_load_3d(sDO + c * C::kBlk, &tmDO, BAR_DOF, c * 64, q0, bh);
+          }
         }
       }
     } else if (warp == kMmaWarp) {
       // ------------------------------------------------------------ UMMA issuer
       if (lane == 0) {
-        constexpr uint32_t idesc_s = idesc_f16(128, 128, BF16, false, false);
+        constexpr uint32_t idesc_s = idesc_f16(128, BQ, BF16, false, false);
         constexpr uint32_t idesc_o = idesc_f16(128, D, BF16, false, true);
-        constexpr uint32_t idesc_q = idesc_f16(128, D, BF16, true, true);
+        constexpr uint32_t idesc_q = idesc_f16(BQ, D, BF16, true, true);  // dQ = dS K
         bool ok = mbar_wait(BAR_KV, 0, abort_flag);
         for (int it = 0; ok && it < steps; ++it) {
           const int st = it & 1;
-          const uint32_t q_base = sQ + st * C::kTile, do_base = sDO + st * C::kTile;
+          const uint32_t q_base = sQ + st * C::kTile;
+          const uint32_t do_base = sDO + (C::kDoStages == 2 ? st : 0) * C::kTile;
+          const int dsb = it % C::kDsBufs;
+          const uint32_t ds_base = sDS + dsb * C::kDsTile;
           if (!mbar_wait(BAR_QF(st), (it >> 1) & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
           // S^T = K Q^T (A = K, B = Q, both K-major)
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_f16_ss(tmem + kColS, sdesc_sw128(sK + off, 16, 1024),
+            const uint32_t off = (kk >> 2) * C::kBlk + (kk & 3) * 32;
+            umma_f16_ss(tmem + C::kColS, sdesc_sw128(sK + off, 16, 1024),
                         sdesc_sw128(q_base + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
           }
           umma_commit(BAR_S);
-          // dP^T = V dO^T, into the columns dQ_{it-1} used: wait for its read-out
-          if (it > 0) {
+          // dP^T = V dO^T; when dQ shares its columns, dQ_{it-1} must have
+          // left TMEM first
+          if (C::kWide && it > 0) {
             if (!mbar_wait(BAR_DQF, (it - 1) & 1, abort_flag)) { ok = false; break; }
-            tc_fence_after();
           }
+          if (C::kDoStages == 1 && !mbar_wait(BAR_DOF, it & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_f16_ss(tmem + kColDP, sdesc_sw128(sV + off, 16, 1024),
+            const uint32_t off = (kk >> 2) * C::kBlk + (kk & 3) * 32;
+            umma_f16_ss(tmem + C::kColDP, sdesc_sw128(sV + off, 16, 1024),
                         sdesc_sw128(do_base + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
           }
           umma_commit(BAR_DP);
-          // dV += P^T dO (A = P^T from TMEM: queries 64h.. packed from column
-          // 64h; B = dO MN-major: rows = queries = K, 64-column blocks of D = N)
+          // dV += P^T dO (A = P^T from TMEM: warp half h packs queries hW..
+          // from column hW; B = dO MN-major: rows = queries = K, 64-column
+          // blocks of D = N)
           if (!mbar_wait(BAR_P, it & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BQ / 16; ++kk)
-            umma_f16_ts(tmem + kColDV, tmem + kColS + (kk >> 2) * 64 + (kk & 3) * 8,
-                        sdesc_sw128(do_base + kk * 2048, 16384, 1024), idesc_o,
+            umma_f16_ts(tmem + C::kColDV, tmem + C::kColS + (kk >> 2) * W + (kk & 3) * 8,
+                        sdesc_sw128(do_base + kk * 2048, C::kBlk, 1024), idesc_o,
                         (it > 0 || kk > 0) ? 1u : 0u);
+          if (C::kDoStages == 1) umma_commit(BAR_DOE);  // dO_it read
           // dK += dS^T Q (A = dS^T K-major: rows = keys, 64-query blocks;
           // B = Q MN-major)
           if (!mbar_wait(BAR_DS, it & 1, abort_flag)) { ok = false; break; }
@@ -316,16 +367,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < BQ / 16; ++kk)
             umma_f16_ss(tmem + C::kColDK,
-                        sdesc_sw128(sDS + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                        sdesc_sw128(q_base + kk * 2048, 16384, 1024), idesc_o,
+                        sdesc_sw128(ds_base + (kk >> 2) * C::kBlk + (kk & 3) * 32, 16, 1024),
+                        sdesc_sw128(q_base + kk * 2048, C::kBlk, 1024), idesc_o,
                         (it > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(BAR_QE(st));  // Q_i / dO_i free once dV and dK have read them
-          // dQ = dS K (A = the dS^T tile read MN-major: rows = keys = K, columns
-          // = queries = M; B = K MN-major: rows = keys = K, columns = D = N)
+          umma_commit(BAR_QE(st));  // Q_it (and dO_it in the ring) read
+          // dQ_{it-1} must have left its own columns before dQ_it
+          if (!C::kWide && it > 0) {
+            if (!mbar_wait(BAR_DQF, (it - 1) & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+          }
+          // dQ = dS K: A = the dS^T tile read MN-major (rows = keys = K,
+          // columns = queries = M); B = the K tile MN-major (rows = keys = K,
+          // 64-column blocks of D = N)
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            umma_f16_ss(tmem + kColDQ, sdesc_sw128(sDS + kk * 2048, 16384, 1024),
-                        sdesc_sw128(sK + kk * 2048, 16384, 1024), idesc_q, kk > 0 ? 1u : 0u);
+            umma_f16_ss(tmem + C::kColDQ, sdesc_sw128(ds_base + kk * 2048, C::kBlk, 1024),
+                        sdesc_sw128(sK + kk * 2048, C::kBlk, 1024), idesc_q, kk > 0 ? 1u : 0u);
+          umma_commit(BAR_DSE(dsb));  // dS^T tile read
           umma_commit(BAR_DQ);
         }
         umma_commit(BAR_FIN);  // dK / dV final (or the pipeline gave up)
@@ -336,46 +394,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     // -------------------------------------------------------------- dQ read-out
     const int row = (warp & 3) * 32 + lane;  // query row of the block = TMEM lane
     const bool issuer = warp == kReadoutWarp0 && lane == 0;
+    int rounds_done = 0;                     // staging rounds committed so far
     for (int it = 0; it < steps; ++it) {
       if (!readout_wait(BAR_DQ, it & 1, abort_flag)) break;
       tc_fence_after();
       const int g = it / nqs, q0 = (i0 + it % nqs) * BQ;
       const int bh = b * H + hkv * G + g;
 #pragma unroll
-      for (int r = 0; r < D / 64; ++r) {
+      for (int r = 0; r < C::kRounds; ++r) {
         float v[64];
-        tmem_ld32(tmem + lane_base + kColDQ + r * 64, v);
-        tmem_ld32(tmem + lane_base + kColDQ + r * 64 + 32, v + 32);
+        tmem_ld32(tmem + lane_base + C::kColDQ + r * 64, v);
+        tmem_ld32(tmem + lane_base + C::kColDQ + r * 64 + 32, v + 32);
         tmem_ld_wait();
-        if (r == D / 64 - 1) {  // dQ fully in registers: its columns are free
+        if (r == C::kRounds - 1) {  // dQ fully out of TMEM: its columns are free
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(BAR_DQF);
         }
-        if (r > 0) {  // staging tile reused: wait until the last reduce read it
-          if (issuer) bulk_wait_group_read<0>();
+        // the staging tile of this round was last read kStBufs rounds ago
+        const int slot = rounds_done % C::kStBufs;
+        if (rounds_done >= C::kStBufs) {
+          if (issuer) bulk_wait_group_read<C::kStBufs - 1>();
           asm volatile("bar.sync 2, 128;" ::: "memory");
         }
+        uint8_t* stg = sp + C::kOffST + slot * C::kStTile;
         // two 32-column boxes, 128-byte swizzled: [box][row][8 chunks of 4 floats]
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const uint32_t addr = (uint32_t)((c >> 3) * 16384) + sw128(row, c & 7);
-          *reinterpret_cast<float4*>(sp + C::kOffDS + addr) =
+        for (int c = 0; c < 16; ++c)
+          *reinterpret_cast<float4*>(stg + (c >> 3) * C::kStBox + sw128(row, c & 7)) =
               make_float4(v[4 * c] * scale, v[4 * c + 1] * scale, v[4 * c + 2] * scale,
                           v[4 * c + 3] * scale);
-        }
         fence_proxy_async_smem();
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (issuer) {
-          tma_reduce_add_3d(&tmDQ, sDS, r * 64, q0, bh);
-          tma_reduce_add_3d(&tmDQ, sDS + 16384, r * 64 + 32, q0, bh);
+          const uint32_t src = sST + slot * C::kStTile;
+          tma_reduce_add_3d(&tmDQ, src, r * 64, q0, bh);
+          tma_reduce_add_3d(&tmDQ, src + C::kStBox, r * 64 + 32, q0, bh);
           bulk_commit_group();
         }
-      }
-      // the staging tile (= the dS^T tile) is free for the next step's dS^T
-      if (issuer) {
-        bulk_wait_group_read<0>();
-        mbar_arrive(BAR_DSF);
+        ++rounds_done;
       }
     }
     if (issuer) bulk_wait_group<0>();  // every dQ reduce has landed
@@ -384,43 +441,51 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ element-wise
     const int krow = (warp & 3) * 32 + lane;  // key row of the block = TMEM lane
     const int key = kv0 + krow;
-    const int h = warp >> 2;                  // query columns 64h .. 64h+63
+    const int h = warp >> 2;                  // query columns hW .. hW+W-1
     bool ok = true;
     for (int it = 0; it < steps; ++it) {
       const int st = it & 1;
       const int q0 = (i0 + it % nqs) * BQ;
-      const float* vec = reinterpret_cast<const float*>(sp + C::kOffVec + st * 1024);
+      const float* vec = reinterpret_cast<const float*>(sp + C::kOffVec + st * C::kVec);
       const bool need_mask = (kv0 + BK > Nk) || (CAUSAL && kv0 + BK - 1 > q0 + koff);
-      // valid iff key <= q + koff: columns c >= qmin of this warp's 64
-      const int qmin = key - koff - (q0 + 64 * h);
-      // the L / D vectors arrived with Q_i (TMA): observe that barrier too
+      // valid iff key <= q + koff: columns c >= qmin of this warp's W
+      const int qmin = key - koff - (q0 + W * h);
+      // the L / D vectors arrived with Q_it (TMA): observe that barrier too
       if (!warp_wait(BAR_QF(st), (it >> 1) & 1, abort_flag)) { ok = false; break; }
       if (!warp_wait(BAR_S, it & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      float p[64];
-      tmem_ld32(tmem + lane_base + kColS + 64 * h, p);
-      tmem_ld32(tmem + lane_base + kColS + 64 * h + 32, p + 32);
+      float p[W];
+      tmem_ld32(tmem + lane_base + C::kColS + W * h, p);
+      tmem_ld32(tmem + lane_base + C::kColS + W * h + 32, p + 32);
       tmem_ld_wait();
-      const float4* l2 = reinterpret_cast<const float4*>(vec + 64 * h);
+      const float4* l2 = reinterpret_cast<const float4*>(vec + W * h);
+      const float2 sc2 = make_float2(scale_log2, scale_log2);
 #pragma unroll
-      for (int c = 0; c < 64; c += 4) {
+      for (int c = 0; c < W; c += 2) {
         const float4 l = l2[c >> 2];
-        p[c] = ex2_mufu(fmaf(p[c], scale_log2, -l.x));
-        p[c + 1] = ex2_mufu(fmaf(p[c + 1], scale_log2, -l.y));
-        p[c + 2] = ex2_mufu(fmaf(p[c + 2], scale_log2, -l.z));
-        p[c + 3] = ex2_mufu(fmaf(p[c + 3], scale_log2, -l.w));
+        const float2 nl = (c & 2) ? make_float2(-l.z, -l.w) : make_float2(-l.x, -l.y);
+        const float2 x = ffma2(make_float2(p[c], p[c + 1]), sc2, nl);
+        float2 e;
+        if (((c >> 1) & 3) < kPolyPairsPer4) {
+          e = exp2_poly2(x);  // FMA pipe
+        } else {
+          e.x = ex2_mufu(x.x);  // MUFU pipe
+          e.y = ex2_mufu(x.y);
+        }
+        p[c] = e.x;
+        p[c + 1] = e.y;
       }
       if (need_mask) {
         const bool key_ok = key < Nk;
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
+        for (int c = 0; c < W; ++c)
           if (!key_ok || (CAUSAL && c < qmin)) p[c] = 0.f;
       }
       {
-        uint32_t pk[32];
+        uint32_t pk[W / 2];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) pk[c] = pack2_u32<BF16>(p[2 * c], p[2 * c + 1]);
-        tmem_st32u(tmem + lane_base + kColS + 64 * h, pk);  // P^T over S^T
+        for (int c = 0; c < W / 2; ++c) pk[c] = pack2_u32<BF16>(p[2 * c], p[2 * c + 1]);
+        tmem_st32u(tmem + lane_base + C::kColS + W * h, pk);  // P^T over this warp's S^T
         tmem_st_wait();
       }
       tc_fence_before();
@@ -429,29 +494,38 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       if (!warp_wait(BAR_DP, it & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      uint32_t ds[32];
-      const float4* dd = reinterpret_cast<const float4*>(vec + 128 + 64 * h);
+      uint32_t ds[W / 2];
+      const float4* dd = reinterpret_cast<const float4*>(vec + BQ + W * h);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      for (int half = 0; half < W / 32; ++half) {
         float dp[32];
-        tmem_ld32(tmem + lane_base + kColDP + 64 * h + 32 * half, dp);
+        tmem_ld32(tmem + lane_base + C::kColDP + W * h + 32 * half, dp);
         tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < 32; c += 4) {
           const float4 d4 = dd[(32 * half + c) >> 2];
           const int pc = 32 * half + c;
-          ds[pc >> 1] = pack2_u32<BF16>(p[pc] * (dp[c] - d4.x), p[pc + 1] * (dp[c + 1] - d4.y));
-          ds[(pc >> 1) + 1] =
-              pack2_u32<BF16>(p[pc + 2] * (dp[c + 2] - d4.z), p[pc + 3] * (dp[c + 3] - d4.w));
+          const float2 a = fmul2(make_float2(p[pc], p[pc + 1]),
+                                 fadd2(make_float2(dp[c], dp[c + 1]), make_float2(-d4.x, -d4.y)));
+          const float2 bq = fmul2(make_float2(p[pc + 2], p[pc + 3]),
+                                  fadd2(make_float2(dp[c + 2], dp[c + 3]), make_float2(-d4.z, -d4.w)));
+          ds[pc >> 1] = pack2_u32<BF16>(a.x, a.y);
+          ds[(pc >> 1) + 1] = pack2_u32<BF16>(bq.x, bq.y);
         }
       }
-      // dP^T has been read (the dQ product may overwrite it after ds_full)
       tc_fence_before();
-      if (it > 0 && !warp_wait(BAR_DSF, (it - 1) & 1, abort_flag)) { ok = false; break; }
-      // dS^T row -> block h of the tile, 8 chunks of 8 queries
+      // the dS^T tile was last read by the products of step it - kDsBufs
+      const int dsb = it % C::kDsBufs;
+      if (it >= C::kDsBufs &&
+          !warp_wait(BAR_DSE(dsb), ((it / C::kDsBufs) - 1) & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      // this warp's W queries = 8 16-byte chunks of row krow, block h
+      uint8_t* dst = sp + C::kOffDS + dsb * C::kDsTile + h * C::kBlk;
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        *reinterpret_cast<uint4*>(sp + C::kOffDS + h * 16384 + sw128(krow, u)) =
+      for (int u = 0; u < W / 8; ++u)
+        *reinterpret_cast<uint4*>(dst + sw128(krow, u)) =
             make_uint4(ds[4 * u], ds[4 * u + 1], ds[4 * u + 2], ds[4 * u + 3]);
       fence_proxy_async_smem();
       __syncwarp();
@@ -462,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && warp_wait(BAR_FIN, 0, abort_flag)) {
       tc_fence_after();
       using T = typename E::T;
-      const uint32_t col = h ? C::kColDK : kColDV;
+      const uint32_t col = h ? C::kColDK : C::kColDV;
       const float mul = h ? scale : 1.f;
       T* out = reinterpret_cast<T*>(h ? dk : dv) + ((size_t)bhk * Nk + key) * D;
 #pragma unroll
@@ -500,7 +574,7 @@ B2A_DEFINE_ERROR_READER(backward)
 // Workspace (fp32): L2 [B*H][Npad], D [B*H][Npad], dQ accumulator [B*H*N*D];
 // Npad = N rounded up to 128 (every region starts 512-byte aligned).
 int64_t backward_workspace_floats(int B, int H, int N, int D) {
-  const int64_t npad = ((int64_t)N + bwd::BQ - 1) / bwd::BQ * bwd::BQ;
+  const int64_t npad = ((int64_t)N + bwd::kPadRows - 1) / bwd::kPadRows * bwd::kPadRows;
   return 2 * (int64_t)B * H * npad + (int64_t)B * H * N * D;
 }
 
@@ -521,7 +595,7 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
     if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(backward)");
     attr_done[dev] = true;
   }
-  const int npad = (N + BQ - 1) / BQ * BQ;
+  const int npad = (N + kPadRows - 1) / kPadRows * kPadRows;
   const long long rows_pad = (long long)B * H * npad;
   float* l2v = ws;
   float* dvec = ws + rows_pad;

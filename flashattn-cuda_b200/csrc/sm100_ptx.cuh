@@ -222,6 +222,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
 __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* r) {
   tmem_st32(taddr, reinterpret_cast<const float*>(r));
 }
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -284,6 +294,15 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
   asm("{\n\t.reg .b64 A, B, D;\n\t"
       "mov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
       "add.rn.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 A, B, D;\n\t"
+      "mov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
+      "mul.rn.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;\n\t}"
       : "=f"(d.x), "=f"(d.y)
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
