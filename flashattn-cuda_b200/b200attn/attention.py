@@ -27,13 +27,45 @@ from . import _lib
 
 _DT = {torch.float16: _lib.B2A_F16, torch.bfloat16: _lib.B2A_BF16}
 
+try:  # CPython binding of b2a_prefill_fwd_kv (same library symbol, cheaper call)
+    from . import _fastcall
+except ImportError:
+    _fastcall = None
+
 
 def _compute_dtype(t: torch.Tensor) -> torch.dtype:
     return t.dtype if t.dtype in _DT else torch.float16
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device) -> int:
+    """The current stream of `device` as a raw cudaStream_t (the reference launches on
+    at::cuda::getCurrentCUDAStream(), cuda/flash_attn_fa3_db_full.cu:380)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def _as(t: torch.Tensor, dt: torch.dtype) -> torch.Tensor:
+    """`t` in dtype `dt`, contiguous (no copy when it already is)."""
+    return t if (t.dtype is dt and t.is_contiguous()) else t.to(dt).contiguous()
+
+
+class _on_device:
+    """Device guard that costs nothing when `device` is already current."""
+
+    def __init__(self, device: torch.device):
+        self.guard = None if device.index == torch.cuda.current_device() else torch.cuda.device(device)
+
+    def __enter__(self):
+        if self.guard is not None:
+            self.guard.__enter__()
+
+    def __exit__(self, *exc):
+        if self.guard is not None:
+            self.guard.__exit__(*exc)
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -62,16 +94,16 @@ def _prefill(Q, K, V, want_L: bool, causal: bool, scale: Optional[float]):
     Hkv = K.shape[1]
     dt = _compute_dtype(Q)
     lib = _lib.load()
-    with torch.cuda.device(Q.device):
-        Qc = Q.to(dt).contiguous()
-        Kc = K.to(dt).contiguous()
-        Vc = V.to(dt).contiguous()
+    with _on_device(Q.device):
+        Qc, Kc, Vc = _as(Q, dt), _as(K, dt), _as(V, dt)
         O = torch.empty((B, H, N, D), dtype=dt, device=Q.device)
         L = torch.empty((B, H, N), dtype=torch.float32, device=Q.device) if want_L else None
         s = float(D) ** -0.5 if scale is None else float(scale)
-        _lib.check(lib.b2a_prefill_fwd_kv(
-            Qc.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), O.data_ptr(), _ptr(L),
-            B, H, Hkv, N, Nk, D, _DT[dt], int(bool(causal)), s, _stream(Q.device)))
+        args = (Qc.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), O.data_ptr(),
+                0 if L is None else L.data_ptr(), B, H, Hkv, N, Nk, D, _DT[dt],
+                int(bool(causal)), s, _stream(Q.device))
+        _lib.check(_fastcall.prefill_fwd_kv(*args) if _fastcall is not None
+                   else lib.b2a_prefill_fwd_kv(*args))
     return O, L
 
 
@@ -125,10 +157,10 @@ def forward_varlen(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
     B = cu_seqlens_q.numel() - 1
     dt = _compute_dtype(Q)
     lib = _lib.load()
-    with torch.cuda.device(Q.device):
-        Qc = Q.to(dt).contiguous()
-        Kc = K.to(dt).contiguous()
-        Vc = V.to(dt).contiguous()
+    with _on_device(Q.device):
+        Qc = _as(Q, dt)
+        Kc = _as(K, dt)
+        Vc = _as(V, dt)
         cq = cu_seqlens_q.contiguous()
         ck = cu_seqlens_k.contiguous()
         O = torch.empty((total_q, H, D), dtype=dt, device=Q.device)
@@ -158,8 +190,8 @@ def backward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, O: torch.Tensor,
         raise RuntimeError("O and dO must have Q's shape, L [B, H, N], V K's shape")
     dt = _compute_dtype(Q)
     lib = _lib.load()
-    with torch.cuda.device(Q.device):
-        Qc, Kc, Vc, Oc, dOc = (t.to(dt).contiguous() for t in (Q, K, V, O, dO))
+    with _on_device(Q.device):
+        Qc, Kc, Vc, Oc, dOc = (_as(t, dt) for t in (Q, K, V, O, dO))
         Lc = L.float().contiguous()
         dQ = torch.empty_like(Qc)
         dK = torch.empty_like(Kc)
@@ -214,10 +246,10 @@ def decode_splitkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, splits: in
         raise RuntimeError("K/V must be [B, Hkv, Lkv, D] with H a multiple of Hkv")
     dt = _compute_dtype(q3)
     lib = _lib.load()
-    with torch.cuda.device(q3.device):
-        qc = q3.to(dt).contiguous()
-        kc = k.to(dt).contiguous()
-        vc = v.to(dt).contiguous()
+    with _on_device(q3.device):
+        qc = _as(q3, dt)
+        kc = _as(k, dt)
+        vc = _as(v, dt)
         o_part = torch.empty((B, H, splits, D), dtype=torch.float32, device=q3.device)
         l_part = torch.empty((B, H, splits), dtype=torch.float32, device=q3.device)
         s = float(D) ** -0.5 if scale is None else float(scale)
@@ -238,7 +270,7 @@ def decode_combine(o_part: torch.Tensor, l_part: torch.Tensor,
         raise RuntimeError("dtype must be torch.float16 or torch.bfloat16")
     B, H, S, D = o_part.shape
     lib = _lib.load()
-    with torch.cuda.device(o_part.device):
+    with _on_device(o_part.device):
         op = o_part.float().contiguous()
         lp = l_part.float().contiguous()
         O = torch.empty((B, H, D), dtype=dtype, device=o_part.device)
@@ -287,10 +319,10 @@ def decode_paged(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
     S = (max_pages + pages_per_split - 1) // pages_per_split
     dt = _compute_dtype(q3)
     lib = _lib.load()
-    with torch.cuda.device(q3.device):
-        qc = q3.to(dt).contiguous()
-        kc = k_pool.to(dt).contiguous()
-        vc = v_pool.to(dt).contiguous()
+    with _on_device(q3.device):
+        qc = _as(q3, dt)
+        kc = _as(k_pool, dt)
+        vc = _as(v_pool, dt)
         bt = block_table.to(torch.int32).contiguous()
         kl = kv_lens.to(torch.int32).contiguous()
         if scratch is None:

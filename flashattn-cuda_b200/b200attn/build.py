@@ -39,6 +39,35 @@ def _sources() -> list[str]:
     return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
 
 
+def _fastcall_path() -> str:
+    import sysconfig
+    return os.path.join(PKG_DIR, "_fastcall" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_fastcall(force: bool = False, verbose: bool = False) -> str | None:
+    """Compile the CPython binding csrc/fastcall.c against libb200attn.so (rpath
+    $ORIGIN).  Returns its path, or None when no C compiler / Python headers exist
+    (the package then calls the library through ctypes only)."""
+    import sysconfig
+    src = os.path.join(CSRC, "fastcall.c")
+    out = _fastcall_path()
+    inc = sysconfig.get_paths()["include"]
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None or not os.path.exists(os.path.join(inc, "Python.h")):
+        return None
+    if not force and not _stale(out, [src, LIB_PATH, os.path.join(INCLUDE, "b200attn.h")]):
+        return out
+    cmd = [cc, "-O2", "-shared", "-fPIC", "-I", inc, src, "-o", out + ".tmp", "-L", PKG_DIR,
+           "-l:libb200attn.so", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"fastcall build failed:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    os.replace(out + ".tmp", out)
+    return out
+
+
 def _deps() -> list[str]:
     hdrs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
     hdrs.append(os.path.join(INCLUDE, "b200attn.h"))
@@ -81,6 +110,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         tmp = LIB_PATH + ".tmp"
         run([nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", tmp, *objs])
         os.replace(tmp, LIB_PATH)
+    build_fastcall(force=force, verbose=verbose)
     return LIB_PATH
 
 

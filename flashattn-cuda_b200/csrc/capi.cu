@@ -103,9 +103,42 @@ int set_cuda_error(cudaError_t e, const char* what) {
   return B2A_ERR_CUDA;
 }
 
+// A tensor map is a pure function of its arguments, so a small per-thread
+// cache of recent encodings (keyed by every argument) saves the host-side
+// encode when a caller reuses its buffers (the usual case in a serving loop).
+namespace {
+struct TmapKey {
+  const void* base;
+  int dt, rank, swz;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3];
+  bool operator==(const TmapKey& o) const { return std::memcmp(this, &o, sizeof *this) == 0; }
+};
+constexpr int kTmapCacheSize = 16;
+thread_local TmapKey t_tmap_keys[kTmapCacheSize];
+thread_local CUtensorMap t_tmap_vals[kTmapCacheSize];
+thread_local int t_tmap_count = 0, t_tmap_next = 0;
+}  // namespace
+
 static int make_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int rank,
                      const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
                      bool swizzle128) {
+  TmapKey key;
+  std::memset(&key, 0, sizeof key);
+  key.base = base;
+  key.dt = (int)dt;
+  key.rank = rank;
+  key.swz = swizzle128 ? 1 : 0;
+  for (int i = 0; i < rank; ++i) {
+    key.dims[i] = dims[i];
+    key.box[i] = box[i];
+  }
+  for (int i = 0; i + 1 < rank; ++i) key.strides[i] = strides[i];
+  for (int i = 0; i < t_tmap_count; ++i)
+    if (t_tmap_keys[i] == key) {
+      *map = t_tmap_vals[i];
+      return B2A_OK;
+    }
   auto fn = encode_fn();
   if (fn == nullptr) return set_error(B2A_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint32_t estr[3] = {1, 1, 1};
@@ -118,6 +151,11 @@ static int make_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dt,
     snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
     return set_error(B2A_ERR_INVALID_ARG, buf);
   }
+  const int slot = t_tmap_next;
+  t_tmap_next = (t_tmap_next + 1) % kTmapCacheSize;
+  if (t_tmap_count < kTmapCacheSize) ++t_tmap_count;
+  t_tmap_keys[slot] = key;
+  t_tmap_vals[slot] = *map;
   return B2A_OK;
 }
 

@@ -55,6 +55,21 @@ def test_no_device_is_reported_not_faulted():
     assert b"sm_100" in lib.b2a_last_error()
 
 
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU failure path")
+def test_fastcall_binding_shares_the_library():
+    """The CPython binding calls the same loaded libb200attn.so as ctypes: an
+    error it triggers is visible through the ctypes handle's b2a_last_error."""
+    from b200attn import _lib
+    import b200attn.attention as A
+    if A._fastcall is None:
+        pytest.skip("CPython binding not built")
+    lib = _lib.load()
+    lib.b2a_status_string(0)
+    rc = A._fastcall.prefill_fwd_kv(0, 0, 0, 0, 0, 1, 1, 1, 64, 64, 64, 0, 0, 0.125, 0)
+    assert rc == 6  # B2A_ERR_NO_DEVICE
+    assert b"sm_100" in lib.b2a_last_error()
+
+
 def test_python_api_rejects_like_the_reference():
     import b200attn
     q = torch.zeros(1, 1, 8, 64, dtype=torch.float16)
