@@ -51,10 +51,10 @@ constexpr int kReadoutWarp0 = 8;
 constexpr int kProducerWarp = 12;
 constexpr int kMmaWarp = 13;
 // Register split: launched at 128 per thread (512 threads), the element-wise
-// warpgroups take 176, the read-out warpgroup 104 and the control warpgroup 56:
-// 256 * 176 + 128 * 104 + 128 * 56 == 512 * 128.
-constexpr uint32_t kRegsElem = 176;
-constexpr uint32_t kRegsReadout = 104;
+// warpgroups take 144, the read-out warpgroup 168 (a whole D = 128 dQ row) and
+// the control warpgroup 56: 256 * 144 + 128 * 168 + 128 * 56 == 512 * 128.
+constexpr uint32_t kRegsElem = 144;
+constexpr uint32_t kRegsReadout = 168;
 constexpr uint32_t kRegsCtrl = 56;
 static_assert(256 * kRegsElem + 128 * kRegsReadout + 128 * kRegsCtrl == kThreads * 128,
               "register split must add up to the launch allocation");
@@ -318,16 +318,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t idesc_s = idesc_f16(128, BQ, BF16, false, false);
         constexpr uint32_t idesc_o = idesc_f16(128, D, BF16, false, true);
         constexpr uint32_t idesc_q = idesc_f16(BQ, D, BF16, true, true);  // dQ = dS K
-        bool ok = mbar_wait(BAR_KV, 0, abort_flag);
-        for (int it = 0; ok && it < steps; ++it) {
-          const int st = it & 1;
-          const uint32_t q_base = sQ + st * C::kTile;
-          const uint32_t do_base = sDO + (C::kDoStages == 2 ? st : 0) * C::kTile;
-          const int dsb = it % C::kDsBufs;
-          const uint32_t ds_base = sDS + dsb * C::kDsTile;
-          if (!mbar_wait(BAR_QF(st), (it >> 1) & 1, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          // S^T = K Q^T (A = K, B = Q, both K-major)
+        // Software-pipelined order: S^T(it+1) is issued right after dV(it), so
+        // the element-wise warps form P^T(it+1) while dQ(it), dK(it) and
+        // dP^T(it+1) run:
+        //   S(0) dP(0) | dV(0) S(1) dQ(0) dK(0) dP(1) | dV(1) S(2) dQ(1) ...
+        auto issue_s = [&](int it) {  // S^T = K Q^T (A = K, B = Q, both K-major)
+          const uint32_t q_base = sQ + (it & 1) * C::kTile;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * C::kBlk + (kk & 3) * 32;
@@ -335,13 +331,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         sdesc_sw128(q_base + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
           }
           umma_commit(BAR_S);
-          // dP^T = V dO^T; when dQ shares its columns, dQ_{it-1} must have
-          // left TMEM first
-          if (C::kWide && it > 0) {
-            if (!mbar_wait(BAR_DQF, (it - 1) & 1, abort_flag)) { ok = false; break; }
-          }
-          if (C::kDoStages == 1 && !mbar_wait(BAR_DOF, it & 1, abort_flag)) { ok = false; break; }
-          tc_fence_after();
+        };
+        auto issue_dp = [&](int it) {  // dP^T = V dO^T (A = V, B = dO, both K-major)
+          const uint32_t do_base = sDO + (C::kDoStages == 2 ? (it & 1) : 0) * C::kTile;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * C::kBlk + (kk & 3) * 32;
@@ -349,6 +341,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                         sdesc_sw128(do_base + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
           }
           umma_commit(BAR_DP);
+        };
+        bool ok = mbar_wait(BAR_KV, 0, abort_flag) && mbar_wait(BAR_QF(0), 0, abort_flag) &&
+                  (C::kDoStages == 2 || mbar_wait(BAR_DOF, 0, abort_flag));
+        if (ok) {
+          tc_fence_after();
+          issue_s(0);
+          issue_dp(0);
+        }
+        for (int it = 0; ok && it < steps; ++it) {
+          const int st = it & 1;
+          const uint32_t q_base = sQ + st * C::kTile;
+          const uint32_t do_base = sDO + (C::kDoStages == 2 ? st : 0) * C::kTile;
+          const int dsb = it % C::kDsBufs;
+          const uint32_t ds_base = sDS + dsb * C::kDsTile;
           // dV += P^T dO (A = P^T from TMEM: warp half h packs queries hW..
           // from column hW; B = dO MN-major: rows = queries = K, 64-column
           // blocks of D = N)
@@ -360,37 +366,71 @@ __global__ void __launch_bounds__(kThreads, 1)
                         sdesc_sw128(do_base + kk * 2048, C::kBlk, 1024), idesc_o,
                         (it > 0 || kk > 0) ? 1u : 0u);
           if (C::kDoStages == 1) umma_commit(BAR_DOE);  // dO_it read
-          // dK += dS^T Q (A = dS^T K-major: rows = keys, 64-query blocks;
-          // B = Q MN-major)
-          if (!mbar_wait(BAR_DS, it & 1, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < BQ / 16; ++kk)
-            umma_f16_ss(tmem + C::kColDK,
-                        sdesc_sw128(ds_base + (kk >> 2) * C::kBlk + (kk & 3) * 32, 16, 1024),
-                        sdesc_sw128(q_base + kk * 2048, C::kBlk, 1024), idesc_o,
-                        (it > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(BAR_QE(st));  // Q_it (and dO_it in the ring) read
-          // dQ_{it-1} must have left its own columns before dQ_it
-          if (!C::kWide && it > 0) {
-            if (!mbar_wait(BAR_DQF, (it - 1) & 1, abort_flag)) { ok = false; break; }
+          // S^T(it+1) over P^T(it), which dV(it) above has already consumed
+          if (it + 1 < steps) {
+            if (!mbar_wait(BAR_QF((it + 1) & 1), ((it + 1) >> 1) & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
             tc_fence_after();
+            issue_s(it + 1);
           }
+          if (!mbar_wait(BAR_DS, it & 1, abort_flag)) { ok = false; break; }
+          // dQ_{it-1} must have left its own columns before dQ_it
+          if (!C::kWide && it > 0 && !mbar_wait(BAR_DQF, (it - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           // dQ = dS K: A = the dS^T tile read MN-major (rows = keys = K,
           // columns = queries = M); B = the K tile MN-major (rows = keys = K,
-          // 64-column blocks of D = N)
+          // 64-column blocks of D = N).  At D = 128 it overwrites dP^T(it),
+          // which the element-wise warps read before ds_full.
+          auto issue_dq = [&]() {
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            umma_f16_ss(tmem + C::kColDQ, sdesc_sw128(ds_base + kk * 2048, C::kBlk, 1024),
-                        sdesc_sw128(sK + kk * 2048, C::kBlk, 1024), idesc_q, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < BK / 16; ++kk)
+              umma_f16_ss(tmem + C::kColDQ, sdesc_sw128(ds_base + kk * 2048, C::kBlk, 1024),
+                          sdesc_sw128(sK + kk * 2048, C::kBlk, 1024), idesc_q, kk > 0 ? 1u : 0u);
+            umma_commit(BAR_DQ);
+          };
+          // dK += dS^T Q (A = dS^T K-major: rows = keys, 64-query blocks;
+          // B = Q MN-major)
+          auto issue_dk = [&]() {
+#pragma unroll
+            for (int kk = 0; kk < BQ / 16; ++kk)
+              umma_f16_ss(tmem + C::kColDK,
+                          sdesc_sw128(ds_base + (kk >> 2) * C::kBlk + (kk & 3) * 32, 16, 1024),
+                          sdesc_sw128(q_base + kk * 2048, C::kBlk, 1024), idesc_o,
+                          (it > 0 || kk > 0) ? 1u : 0u);
+          };
+          // At D = 128 the dQ read-out gates the next dP^T (shared columns):
+          // dQ first.  At D = 64 dQ has its own columns: dK first, which gives
+          // the read-out of dQ(it-1) longer before dQ(it) needs its columns.
+          if (C::kWide) {
+            issue_dq();
+            issue_dk();
+          } else {
+            issue_dk();
+            issue_dq();
+          }
+          umma_commit(BAR_QE(st));    // Q_it (and dO_it in the ring) read
           umma_commit(BAR_DSE(dsb));  // dS^T tile read
-          umma_commit(BAR_DQ);
+          // dP^T(it+1): at D = 128 into the dQ columns once dQ(it) has left them
+          if (it + 1 < steps) {
+            if (C::kWide && !mbar_wait(BAR_DQF, it & 1, abort_flag)) { ok = false; break; }
+            if (C::kDoStages == 1 && !mbar_wait(BAR_DOF, (it + 1) & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_dp(it + 1);
+          }
         }
         umma_commit(BAR_FIN);  // dK / dV final (or the pipeline gave up)
       }
     }
   } else if (warp >= kReadoutWarp0) {
-    setmaxnreg_dec<kRegsReadout>();
+    setmaxnreg_inc<kRegsReadout>();
     // -------------------------------------------------------------- dQ read-out
     const int row = (warp & 3) * 32 + lane;  // query row of the block = TMEM lane
     const bool issuer = warp == kReadoutWarp0 && lane == 0;
@@ -400,17 +440,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int g = it / nqs, q0 = (i0 + it % nqs) * BQ;
       const int bh = b * H + hkv * G + g;
+      // the whole dQ row into registers first, so its TMEM columns free at once
+      float v[D];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) tmem_ld32(tmem + lane_base + C::kColDQ + c * 32, v + 32 * c);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR_DQF);
 #pragma unroll
       for (int r = 0; r < C::kRounds; ++r) {
-        float v[64];
-        tmem_ld32(tmem + lane_base + C::kColDQ + r * 64, v);
-        tmem_ld32(tmem + lane_base + C::kColDQ + r * 64 + 32, v + 32);
-        tmem_ld_wait();
-        if (r == C::kRounds - 1) {  // dQ fully out of TMEM: its columns are free
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(BAR_DQF);
-        }
         // the staging tile of this round was last read kStBufs rounds ago
         const int slot = rounds_done % C::kStBufs;
         if (rounds_done >= C::kStBufs) {
@@ -419,11 +458,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint8_t* stg = sp + C::kOffST + slot * C::kStTile;
         // two 32-column boxes, 128-byte swizzled: [box][row][8 chunks of 4 floats]
+        const float* vr = v + 64 * r;
 #pragma unroll
         for (int c = 0; c < 16; ++c)
           *reinterpret_cast<float4*>(stg + (c >> 3) * C::kStBox + sw128(row, c & 7)) =
-              make_float4(v[4 * c] * scale, v[4 * c + 1] * scale, v[4 * c + 2] * scale,
-                          v[4 * c + 3] * scale);
+              make_float4(vr[4 * c] * scale, vr[4 * c + 1] * scale, vr[4 * c + 2] * scale,
+                          vr[4 * c + 3] * scale);
         fence_proxy_async_smem();
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (issuer) {
@@ -493,14 +533,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(BAR_P);
 
       if (!warp_wait(BAR_DP, it & 1, abort_flag)) { ok = false; break; }
+      // the dS^T tile was last read by the products of step it - kDsBufs
+      const int dsb = it % C::kDsBufs;
+      if (it >= C::kDsBufs &&
+          !warp_wait(BAR_DSE(dsb), ((it / C::kDsBufs) - 1) & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      uint32_t ds[W / 2];
       const float4* dd = reinterpret_cast<const float4*>(vec + BQ + W * h);
+      // this warp's W queries = 8 16-byte chunks of row krow in block h,
+      // formed and stored 32 queries (4 chunks) at a time
+      uint8_t* dst = sp + C::kOffDS + dsb * C::kDsTile + h * C::kBlk;
 #pragma unroll
       for (int half = 0; half < W / 32; ++half) {
         float dp[32];
         tmem_ld32(tmem + lane_base + C::kColDP + W * h + 32 * half, dp);
         tmem_ld_wait();
+        uint32_t ds[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 4) {
           const float4 d4 = dd[(32 * half + c) >> 2];
@@ -509,24 +559,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  fadd2(make_float2(dp[c], dp[c + 1]), make_float2(-d4.x, -d4.y)));
           const float2 bq = fmul2(make_float2(p[pc + 2], p[pc + 3]),
                                   fadd2(make_float2(dp[c + 2], dp[c + 3]), make_float2(-d4.z, -d4.w)));
-          ds[pc >> 1] = pack2_u32<BF16>(a.x, a.y);
-          ds[(pc >> 1) + 1] = pack2_u32<BF16>(bq.x, bq.y);
+          ds[c >> 1] = pack2_u32<BF16>(a.x, a.y);
+          ds[(c >> 1) + 1] = pack2_u32<BF16>(bq.x, bq.y);
         }
-      }
-      tc_fence_before();
-      // the dS^T tile was last read by the products of step it - kDsBufs
-      const int dsb = it % C::kDsBufs;
-      if (it >= C::kDsBufs &&
-          !warp_wait(BAR_DSE(dsb), ((it / C::kDsBufs) - 1) & 1, abort_flag)) {
-        ok = false;
-        break;
-      }
-      // this warp's W queries = 8 16-byte chunks of row krow, block h
-      uint8_t* dst = sp + C::kOffDS + dsb * C::kDsTile + h * C::kBlk;
 #pragma unroll
-      for (int u = 0; u < W / 8; ++u)
-        *reinterpret_cast<uint4*>(dst + sw128(krow, u)) =
-            make_uint4(ds[4 * u], ds[4 * u + 1], ds[4 * u + 2], ds[4 * u + 3]);
+        for (int u = 0; u < 4; ++u)
+          *reinterpret_cast<uint4*>(dst + sw128(krow, 4 * half + u)) =
+              make_uint4(ds[4 * u], ds[4 * u + 1], ds[4 * u + 2], ds[4 * u + 3]);
+      }
+      // dP^T has been read (the dQ product may overwrite it after ds_full)
+      tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR_DS);
