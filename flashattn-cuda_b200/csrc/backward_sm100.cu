@@ -393,26 +393,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                           sdesc_sw128(sK + kk * 2048, C::kBlk, 1024), idesc_q, kk > 0 ? 1u : 0u);
             umma_commit(BAR_DQ);
           };
-          // dK += dS^T Q (A = dS^T K-major: rows = keys, 64-query blocks;
-          // B = Q MN-major)
-          auto issue_dk = [&]() {
+          // dK += dS^T Q (TS: A = dS^T packed over the dP^T columns by the
+          // element-wise warps, like P^T over S^T; B = Q MN-major).  dK reads
+          // those columns, so it goes before dQ, which overwrites them at D = 128.
 #pragma unroll
-            for (int kk = 0; kk < BQ / 16; ++kk)
-              umma_f16_ss(tmem + C::kColDK,
-                          sdesc_sw128(ds_base + (kk >> 2) * C::kBlk + (kk & 3) * 32, 16, 1024),
-                          sdesc_sw128(q_base + kk * 2048, C::kBlk, 1024), idesc_o,
-                          (it > 0 || kk > 0) ? 1u : 0u);
-          };
-          // At D = 128 the dQ read-out gates the next dP^T (shared columns):
-          // dQ first.  At D = 64 dQ has its own columns: dK first, which gives
-          // the read-out of dQ(it-1) longer before dQ(it) needs its columns.
-          if (C::kWide) {
-            issue_dq();
-            issue_dk();
-          } else {
-            issue_dk();
-            issue_dq();
-          }
+          for (int kk = 0; kk < BQ / 16; ++kk)
+            umma_f16_ts(tmem + C::kColDK, tmem + C::kColDP + (kk >> 2) * W + (kk & 3) * 8,
+                        sdesc_sw128(q_base + kk * 2048, C::kBlk, 1024), idesc_o,
+                        (it > 0 || kk > 0) ? 1u : 0u);
+          issue_dq();
           umma_commit(BAR_QE(st));    // Q_it (and dO_it in the ring) read
           umma_commit(BAR_DSE(dsb));  // dS^T tile read
           // dP^T(it+1): at D = 128 into the dQ columns once dQ(it) has left them
@@ -566,7 +555,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int u = 0; u < 4; ++u)
           *reinterpret_cast<uint4*>(dst + sw128(krow, 4 * half + u)) =
               make_uint4(ds[4 * u], ds[4 * u + 1], ds[4 * u + 2], ds[4 * u + 3]);
+        // and packed over the dP^T columns just read (the A operand of dK)
+        tmem_st16u(tmem + lane_base + C::kColDP + W * h + 16 * half, ds);
       }
+      tmem_st_wait();
       // dP^T has been read (the dQ product may overwrite it after ds_full)
       tc_fence_before();
       fence_proxy_async_smem();
