@@ -506,19 +506,34 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
+    def keep_busy(samples_wanted: int):
+        """Run untimed steps until the clock sampler has `samples_wanted` more
+        samples (at most ~3 s).  Every rank runs the same number of steps: a
+        step may contain a collective (KV-sharded decode), so the ranks agree on
+        each round through a one-element MAX all-reduce instead of deciding
+        from their own sampler."""
+        t_end = time.time() + 3.0
+        n = sampler.count()
+        while True:
+            more = (sampler.proc is not None and sampler.count() < n + samples_wanted
+                    and time.time() < t_end)
+            if world > 1:
+                flag = torch.tensor([1 if more else 0], dtype=torch.int32, device=dev)
+                dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+                more = bool(flag.item())
+            if not more:
+                return
+            for i in range(4):
+                step(i)
+            torch.cuda.synchronize(dev)
+
     # ---- warm-up, started after the clock sampler so that the GPU is not left
     # idle between the warm-up and the timed region
     sampler = ClockSampler(local_rank)
     sampler.start()
     for i in range(args.warmup):
         step(i)
-    # keep the GPU busy until the sampler is producing samples (at most ~3 s)
-    t_end = time.time() + 3.0
-    n0 = sampler.count()
-    while sampler.proc is not None and sampler.count() < n0 + 2 and time.time() < t_end:
-        for i in range(4):
-            step(i)
-        torch.cuda.synchronize(dev)
+    keep_busy(2)  # until the sampler is producing samples
 
     # ---- timed device-resident region (barrier + synchronize on both sides)
     barrier()
@@ -533,12 +548,7 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     ms = ev0.elapsed_time(ev1)
     # and keep it busy (untimed) until a sample after the timed region lands
-    t_end = time.time() + 3.0
-    n1 = sampler.count()
-    while sampler.proc is not None and sampler.count() < n1 + 1 and time.time() < t_end:
-        for i in range(4):
-            step(i)
-        torch.cuda.synchronize(dev)
+    keep_busy(1)
     clocks = sampler.stop()
 
     # ---- per-step device time of the dominant kernel(s), for the roofline: a
