@@ -74,6 +74,11 @@ CONFIGS = {
               causal=True, shard=True,
               name="varlen prefill fwd: 16 packed sequences len U[256,8192] H=32 Hkv=8 D=128 "
                    "bf16 causal"),
+    # config 6 with 4 sequences (~230 MB of Q/K/V, > L2): the case ncu captures run on
+    "6s": dict(kind="varlen", B=4, H=32, Hkv=8, D=128, lmin=256, lmax=8192, dtype="bfloat16",
+               causal=True, shard=True,
+               name="varlen prefill fwd: 4 packed sequences len U[256,8192] H=32 Hkv=8 D=128 "
+                    "bf16 causal (config 6, small)"),
 }
 
 

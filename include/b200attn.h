@@ -108,7 +108,8 @@ int b2a_backward(const void* q, const void* k, const void* v, const void* o,
                  void* dv, float* workspace, int B, int H, int Hkv, int N,
                  int Nk, int D, int dtype, int causal, float scale,
                  void* stream);
-/* Floats of workspace b2a_backward needs. */
+/* Floats of workspace b2a_backward needs: 2*B*H*Npad (row statistics, Npad =
+ * N rounded up to 128) + B*H*N*D (the fp32 dQ accumulator). */
 int64_t b2a_backward_workspace_floats(int B, int H, int N, int D);
 
 /*
