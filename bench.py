@@ -56,7 +56,7 @@ CONFIGS = {
     # config 4 at 1/8 batch (537 MB of KV, still > L2): the case ncu section captures run on
     "4s": dict(kind="decode", B=8, H=32, Hkv=8, L=16384, D=128, dtype="float16", splits=16,
                shard=True, name="config4-small: split-KV GQA decode B=8 H=32 Hkv=8 L=16384 D=128 fp16"),
-    "5b": dict(kind="kvshard", B=1, H=32, Hkv=8, L=131072, D=128, dtype="bfloat16", splits=64,
+    "5b": dict(kind="kvshard", B=1, H=32, Hkv=8, L=131072, D=128, dtype="bfloat16", splits=32,
                shard=True, name="config5b: KV-sharded decode B=1 H=32 Hkv=8 L=131072 D=128 bf16, "
                                 "NCCL all-gather of partials"),
     "5a": dict(kind="paged", B=128, H=32, Hkv=8, D=128, page=16, lmin=512, lmax=32768,
