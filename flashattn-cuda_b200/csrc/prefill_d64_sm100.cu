@@ -54,8 +54,8 @@ constexpr uint32_t kOffK = kOffQ + 2 * kQBytes;
 constexpr uint32_t kOffV = kOffK + kStages * kKVBytes;
 constexpr uint32_t kOffML = kOffV + kStages * kKVBytes;  // epilogue exchange: [2][2][128] x (m, l)
 constexpr uint32_t kOffBar = kOffML + 2 * 2 * 128 * 8;
-// q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2][2], pv_done[2][2], epi[2]
-constexpr int kNumBars = 1 + 3 * kStages + 2 + 4 + 4 + 2;
+// q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2][2], pv_done[2], epi[2]
+constexpr int kNumBars = 1 + 3 * kStages + 2 + 4 + 2 + 2;
 constexpr uint32_t kOffTmemSlot = kOffBar + 8 * kNumBars;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 8;
 constexpr uint32_t kSmemBytes = kOffAbort + 8 + 1024;
@@ -81,8 +81,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto BAR_KVE = [&](int s) { return bar0 + 8u * (1 + 2 * S + s); };
   auto BAR_SF = [&](int t) { return bar0 + 8u * (1 + 3 * S + t); };
   auto BAR_PF = [&](int t, int h) { return bar0 + 8u * (3 + 3 * S + 2 * t + h); };
-  auto BAR_PVD = [&](int t, int h) { return bar0 + 8u * (7 + 3 * S + 2 * t + h); };
-  auto BAR_EPI = [&](int t) { return bar0 + 8u * (11 + 3 * S + t); };
+  auto BAR_PVD = [&](int t) { return bar0 + 8u * (7 + 3 * S + t); };
+  auto BAR_EPI = [&](int t) { return bar0 + 8u * (9 + 3 * S + t); };
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sp + kOffTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sp + kOffAbort);
   float2* s_ml = reinterpret_cast<float2*>(sp + kOffML);  // [t][h][row]
@@ -151,13 +151,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dq0 = sdesc_sw128(sQ, 16, 1024);
       const uint64_t dk0 = sdesc_sw128(sK, 16, 1024);
       const uint64_t dv0 = sdesc_sw128(sV, 16, 1024);  // N = 64: one column block
+      // Every commit point costs the tensor pipe a bubble of ~100 clocks, so each
+      // Q tile's two PV products and its next S are issued as one run with one
+      // commit point (pv_done and s_full committed back to back).
       auto issue_s = [&](int t, int j) {
         const uint64_t qd = dq0 + ((t * kQBytes) >> 4);
         const uint64_t kd = dk0 + (((j % S) * kKVBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           umma_f16_ss(tmem + t * 128, qd + kk * 2, kd + kk * 2, idesc_qk, kk > 0 ? 1u : 0u);
-        umma_commit(BAR_SF(t));
       };
       auto issue_pv = [&](int t, int h, int j) {
         const uint64_t vd = dv0 + (((j % S) * kKVBytes + h * HALF * 128) >> 4);
@@ -166,13 +168,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < HALF / 16; ++kk)
           umma_f16_ts(d_o, a_p + kk * 8, vd + kk * 128, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(BAR_PVD(t, h));
       };
       bool ok = mbar_wait(BAR_Q, 0, abort_flag) && mbar_wait(BAR_KF(0), 0, abort_flag);
       if (ok) {
         tc_fence_after();
         issue_s(0, 0);
+        umma_commit(BAR_SF(0));
         issue_s(1, 0);
+        umma_commit(BAR_SF(1));
       }
       for (int j = 0; ok && j < nkv; ++j) {
         const int st = j % S;
@@ -187,7 +190,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             issue_pv(t, h, j);
           }
-          if (ok && j + 1 < nkv_t[t]) {  // S_t(j+1) overwrites P_{t,*}(j): after both PVs
+          if (!ok) break;
+          const bool s_next = j + 1 < nkv_t[t];
+          if (s_next) {  // S_t(j+1) overwrites P_{t,*}(j): after both PVs
             if (!k_next) {
               if (!mbar_wait(BAR_KF((j + 1) % S), ((j + 1) / S) & 1, abort_flag)) {
                 ok = false;
@@ -198,6 +203,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             issue_s(t, j + 1);
           }
+          umma_commit(BAR_PVD(t));
+          if (s_next) umma_commit(BAR_SF(t));
         }
         umma_commit(BAR_KVE(st));
       }
@@ -273,9 +280,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // P_{t,h}(j) over this half of S_t (32 packed columns)
       tmem_st32u(t_s, pk);
-      // O_{t,h} is still accumulated by PV_{t,h}(j-1): rescale once that is done
+      // O_{t,h} is still accumulated by the PV products of step j-1: rescale once
+      // they are done
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-        if (!mbar_wait(BAR_PVD(t, h), (j - 1) & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(BAR_PVD(t), (j - 1) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
@@ -297,12 +305,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // exchange (m, l) with the other half of the row, then merge:
     //   M = max(m0, m1), w_i = 2^(m_i - M), L = l0 w0 + l1 w1,
     //   O = (w0 O_{t,0} + w1 O_{t,1}) / L   (this thread: columns [32h, 32h+32))
-    if (ok) ok = mbar_wait(BAR_PVD(t, h), (my_nkv - 1) & 1, abort_flag);
+    if (ok) ok = mbar_wait(BAR_PVD(t), (my_nkv - 1) & 1, abort_flag);
     s_ml[(t * 2 + h) * 128 + row] = make_float2(ok ? m_run : -INFINITY, ok ? l_run : 0.f);
     __syncwarp();
     if (lane == 0) mbar_arrive(BAR_EPI(t));
     if (ok) ok = mbar_wait(BAR_EPI(t), 0, abort_flag);
-    if (ok) ok = mbar_wait(BAR_PVD(t, 1 - h), (my_nkv - 1) & 1, abort_flag);
     if (ok) {
       tc_fence_after();
       const float2 ml0 = s_ml[(t * 2 + 0) * 128 + row];

@@ -218,7 +218,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t bd = sdesc_sw128(k_base + off, 16, 1024);
             umma_f16_ss(tmem + t * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
           }
-          umma_commit(BAR_SF(t));
         };
         auto issue_pv = [&](int t, int j) {
           const uint32_t v_base = sV + (j % S) * C::kKVBytes;
@@ -228,13 +227,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_f16_ts(tmem + C::kTmemO + t * D, tmem + t * 128 + kk * 8, bd, idesc_pv,
                         (j > 0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(BAR_PVD(t));
         };
         if (ok) ok = mbar_wait(BAR_KF(0), 0, abort_flag);
         if (ok) {
           tc_fence_after();
           issue_s(0, 0);
+          umma_commit(BAR_SF(0));
           issue_s(1, 0);
+          umma_commit(BAR_SF(1));
         }
         for (int j = 0; ok && j < nkv; ++j) {
           const int st = j % S;
@@ -246,7 +246,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!mbar_wait(BAR_PF(t), j & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
             issue_pv(t, j);
-            if (j + 1 < nkv_t[t]) {
+            // PV_t(j) and S_t(j+1) share one commit point: every commit point
+            // costs the tensor pipe a bubble of ~100 clocks
+            const bool s_next = j + 1 < nkv_t[t];
+            if (s_next) {
               if (!k_next_ready) {
                 if (!mbar_wait(BAR_KF((j + 1) % S), ((j + 1) / S) & 1, abort_flag)) {
                   ok = false;
@@ -257,6 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
               issue_s(t, j + 1);
             }
+            umma_commit(BAR_PVD(t));
+            if (s_next) umma_commit(BAR_SF(t));
           }
           umma_commit(BAR_KVE(st));  // K_j / V_j free once every MMA above has run
         }
