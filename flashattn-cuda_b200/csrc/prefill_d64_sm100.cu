@@ -60,13 +60,27 @@ constexpr uint32_t kOffTmemSlot = kOffBar + 8 * kNumBars;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 8;
 constexpr uint32_t kSmemBytes = kOffAbort + 8 + 1024;
 constexpr int kPolyPairsPer8 = 3;  // of 8 exponential pairs, on the FMA pipe
+// Split-KV form (small grids): each CTA's partial O (fp32, normalised by its
+// own sum, rows padded to 68 floats so that a warp's row-strided 16-B stores
+// hit distinct banks) and its per-row (m, l), written over the drained K/V ring.
+constexpr int kPartStride = D + 4;
+constexpr uint32_t kOffPartO = kOffK;
+constexpr uint32_t kOffPartML = kOffPartO + kRowsPerCta * kPartStride * 4;
+static_assert(kOffPartML + kRowsPerCta * 8 <= kOffML, "split partials must fit in the K/V ring");
+constexpr int kMaxSplits = 8;
 
-template <bool BF16, bool CAUSAL>
+// SPLIT (non-causal only): a cluster of `splits` CTAs along x shares one
+// 256-row block; CTA rank r takes KV tiles [r * kv_per_split, ...) and the
+// partial results are merged through distributed shared memory at the end
+// (the LSE-weighted combine of the split-KV decode, done in-kernel).
+template <bool BF16, bool CAUSAL, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_d64_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, void* __restrict__ out,
-                       float* __restrict__ lse, int N, int Nk, int H, int group, float scale_log2) {
+                       float* __restrict__ lse, int N, int Nk, int H, int group, float scale_log2,
+                       int splits, int kv_per_split) {
+  static_assert(!(SPLIT && CAUSAL), "the split-KV form is non-causal");
   using E = Elem<BF16>;
   constexpr int S = kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -89,17 +103,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
+  const int bh = SPLIT ? (int)blockIdx.x / splits : (int)blockIdx.x;
+  const uint32_t crank = SPLIT ? cluster_ctarank() : 0u;
   const int bhk = (bh / H) * (H / group) + (bh % H) / group;
   const int q0 = ((int)gridDim.y - 1 - (int)blockIdx.y) * kRowsPerCta;
   // keys: Nk (>= N when causal); the causal mask is aligned to the bottom
   // right, query row r sees keys <= r + (Nk - N)
   const int koff = Nk - N;
   const int nkv_all = (Nk + BN - 1) / BN;
+  // this CTA's KV tiles: kv_base + [0, nkv_t[t]) for Q tile t (every loop below
+  // runs over the local index j; kv_base + j is the tile's place in the sequence)
+  const int kv_base = SPLIT ? (int)crank * kv_per_split : 0;
   int nkv_t[2];
 #pragma unroll
   for (int t = 0; t < 2; ++t)
-    nkv_t[t] = CAUSAL ? min(nkv_all, (q0 + (t + 1) * BM + koff + BN - 1) / BN) : nkv_all;
+    nkv_t[t] = SPLIT ? min(kv_per_split, nkv_all - kv_base)
+               : CAUSAL ? min(nkv_all, (q0 + (t + 1) * BM + koff + BN - 1) / BN)
+                        : nkv_all;
   const int nkv = nkv_t[1];
 
   if (warp == kProducerWarp && lane == 0) {
@@ -140,9 +160,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = j % S;
         if (j >= S && !mbar_wait(BAR_KVE(st), ((j / S) - 1) & 1, abort_flag)) break;
         mbar_arrive_expect_tx(BAR_KF(st), kKVBytes);
-        tma_load_3d(sK + st * kKVBytes, &tmK, BAR_KF(st), 0, j * BN, bhk);
+        tma_load_3d(sK + st * kKVBytes, &tmK, BAR_KF(st), 0, (kv_base + j) * BN, bhk);
         mbar_arrive_expect_tx(BAR_VF(st), kKVBytes);
-        tma_load_3d(sV + st * kKVBytes, &tmV, BAR_VF(st), 0, j * BN, bhk);
+        tma_load_3d(sV + st * kKVBytes, &tmV, BAR_VF(st), 0, (kv_base + j) * BN, bhk);
       }
     } else if (warp == kMmaWarp && lane == 0) {
       // ---------------------------------------------------------- UMMA issuer
@@ -209,6 +229,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(BAR_KVE(st));
       }
     }
+    if constexpr (SPLIT) {
+      __syncwarp();
+      cluster_sync_all();
+      cluster_sync_all();
+    }
   } else {
     setmaxnreg_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax (t, h)
@@ -231,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(t_s + 32, s + 32);
       tmem_ld_wait();
 
-      const int kv0 = j * BN + h * HALF;
+      const int kv0 = (kv_base + j) * BN + h * HALF;
       const bool need_mask = (kv0 + HALF > Nk) || (CAUSAL && kv0 + HALF > q0 + t * BM + koff);
       if (need_mask) {
         const int lim = (CAUSAL ? min(Nk, grow + 1 + koff) : Nk) - kv0;
@@ -326,7 +351,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(o0, a);
       tmem_ld32(o1, b);
       tmem_ld_wait();
-      if (grow < N) {
+      if constexpr (SPLIT) {
+        // this CTA's partial for the row: O normalised by its own sum, and (M, L)
+        // (the K/V ring is free once both Q tiles' products have run)
+        ok = mbar_wait(BAR_PVD(1 - t), (nkv_t[1 - t] - 1) & 1, abort_flag);
+        float* po = reinterpret_cast<float*>(sp + kOffPartO) + (t * BM + row) * kPartStride + 32 * h;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(po + i) =
+              make_float4(a[i] * f0 + b[i] * f1, a[i + 1] * f0 + b[i + 1] * f1,
+                          a[i + 2] * f0 + b[i + 2] * f1, a[i + 3] * f0 + b[i + 3] * f1);
+        if (h == 0) reinterpret_cast<float2*>(sp + kOffPartML)[t * BM + row] = make_float2(M, Lsum);
+      } else if (grow < N) {
         typename E::T* orow =
             reinterpret_cast<typename E::T*>(out) + ((size_t)bh * N + grow) * D + 32 * h;
 #pragma unroll
@@ -342,6 +378,47 @@ __global__ void __launch_bounds__(kThreads, 1)
           lse[(size_t)bh * N + grow] = M * 0.69314718055994531f + logf(Lsum);
       }
     }
+    if constexpr (SPLIT) {
+      // merge the cluster's partials, this CTA taking rows [crank * rows_per, ...):
+      //   M* = max_c M_c, W_c = L_c 2^(M_c - M*), O = sum_c W_c O_c / sum_c W_c,
+      //   L = M* ln 2 + ln sum_c W_c
+      __syncwarp();
+      cluster_sync_all();  // every CTA's partials are written
+      const int rows_per = kRowsPerCta / splits;
+      const uint32_t po_base = sb + kOffPartO, pml_base = sb + kOffPartML;
+      for (int it = threadIdx.x; it < rows_per * (D / 4); it += kSoftmaxWGs * 128) {
+        const int r = (int)crank * rows_per + it / (D / 4);
+        const int c4 = (it % (D / 4)) * 4;
+        float mx = -INFINITY;
+        for (int c = 0; c < splits; ++c)
+          mx = fmaxf(mx, ld_dsmem_f2(mapa_shared(pml_base + r * 8, (uint32_t)c)).x);
+        float lt = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = 0; c < splits; ++c) {
+          const float2 ml = ld_dsmem_f2(mapa_shared(pml_base + r * 8, (uint32_t)c));
+          const float w = (ml.x == -INFINITY) ? 0.f : ml.y * ex2_mufu(ml.x - mx);
+          const float4 o =
+              ld_dsmem_f4(mapa_shared(po_base + (r * kPartStride + c4) * 4, (uint32_t)c));
+          lt += w;
+          acc.x += w * o.x;
+          acc.y += w * o.y;
+          acc.z += w * o.z;
+          acc.w += w * o.w;
+        }
+        const int qrow = q0 + r;
+        if (qrow < N) {
+          const float inv = 1.f / lt;
+          uint2 wv;
+          wv.x = pack2_u32<BF16>(acc.x * inv, acc.y * inv);
+          wv.y = pack2_u32<BF16>(acc.z * inv, acc.w * inv);
+          *reinterpret_cast<uint2*>(reinterpret_cast<typename E::T*>(out) +
+                                    ((size_t)bh * N + qrow) * D + c4) = wv;
+          if (c4 == 0 && lse != nullptr)
+            lse[(size_t)bh * N + qrow] = mx * 0.69314718055994531f + logf(lt);
+        }
+      }
+      cluster_sync_all();  // no CTA leaves while a peer still reads its partials
+    }
   }
 
   tc_fence_before();
@@ -354,11 +431,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace prefill64
 
-template <bool BF16, bool CAUSAL>
+template <bool BF16, bool CAUSAL, bool SPLIT>
 static int launch_prefill_d64(const void* q, const void* k, const void* v, void* o, float* lse,
-                              int B, int H, int Hkv, int N, int Nk, float scale, cudaStream_t stream) {
+                              int B, int H, int Hkv, int N, int Nk, float scale, int splits,
+                              cudaStream_t stream) {
   using namespace prefill64;
-  auto kern = prefill_d64_kernel<BF16, CAUSAL>;
+  auto kern = prefill_d64_kernel<BF16, CAUSAL, SPLIT>;
   static bool attr_done[kMaxDevices] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
@@ -376,24 +454,73 @@ static int launch_prefill_d64(const void* q, const void* k, const void* v, void*
   if (rc == B2A_OK) rc = make_tmap_3d(&tk, k, dt, D, Nk, (uint64_t)B * Hkv, 64, BN, true);
   if (rc == B2A_OK) rc = make_tmap_3d(&tv, v, dt, D, Nk, (uint64_t)B * Hkv, 64, BN, true);
   if (rc != B2A_OK) return rc;
-  dim3 grid((unsigned)(B * H), (unsigned)((N + kRowsPerCta - 1) / kRowsPerCta));
-  kern<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, o, lse, N, Nk, H, H / Hkv,
-                                               scale * 1.4426950408889634f);
-  cudaError_t e = cudaGetLastError();
+  const unsigned blocks = (unsigned)((N + kRowsPerCta - 1) / kRowsPerCta);
+  const float scale_log2 = scale * 1.4426950408889634f;
+  cudaError_t e;
+  if constexpr (SPLIT) {
+    const int nkv = (Nk + BN - 1) / BN;
+    const int per = (nkv + splits - 1) / splits;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(B * H * splits), blocks, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, o, lse, N, Nk, H, H / Hkv, scale_log2, splits,
+                           per);
+  } else {
+    dim3 grid((unsigned)(B * H), blocks);
+    kern<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, o, lse, N, Nk, H, H / Hkv, scale_log2,
+                                                 1, 0);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) return set_cuda_error(e, "prefill d64 kernel launch");
   return B2A_OK;
+}
+
+// Split-KV factor for a non-causal launch: the largest power of two <= 8 whose
+// clusters still fit in one wave on the device's SMs and give every split at
+// least one KV tile; 1 (no split) when the plain grid already fills the GPU.
+static int d64_splits(int B, int H, int N, int Nk) {
+  static int sms[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 1;
+  if (sms[dev] == 0 &&
+      cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 1;
+  const int64_t ctas = (int64_t)B * H * ((N + prefill64::kRowsPerCta - 1) / prefill64::kRowsPerCta);
+  const int nkv = (Nk + prefill64::BN - 1) / prefill64::BN;
+  for (int s = prefill64::kMaxSplits; s >= 2; s >>= 1) {
+    if (ctas * s > sms[dev]) continue;
+    const int per = (nkv + s - 1) / s;
+    if ((s - 1) * per < nkv) return s;
+  }
+  return 1;
 }
 
 int prefill_d64_dispatch(const void* q, const void* k, const void* v, void* o, float* lse, int B,
                          int H, int Hkv, int N, int Nk, int dtype, int causal, float scale,
                          cudaStream_t stream) {
   const bool bf = dtype == B2A_BF16;
-  if (bf) {
-    return causal ? launch_prefill_d64<true, true>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, stream)
-                  : launch_prefill_d64<true, false>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, stream);
-  }
-  return causal ? launch_prefill_d64<false, true>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, stream)
-                : launch_prefill_d64<false, false>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, stream);
+  const int splits = causal ? 1 : d64_splits(B, H, N, Nk);
+#define B2A_D64(BB, CC, SS)                                                                      \
+  if (bf == BB && (causal != 0) == CC && (splits > 1) == SS)                                    \
+    return launch_prefill_d64<BB, CC, SS>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, splits,   \
+                                          stream);
+  B2A_D64(false, false, false)
+  B2A_D64(false, false, true)
+  B2A_D64(false, true, false)
+  B2A_D64(true, false, false)
+  B2A_D64(true, false, true)
+  B2A_D64(true, true, false)
+#undef B2A_D64
+  return set_error(B2A_ERR_UNSUPPORTED, "prefill d64: no kernel for this configuration");
 }
 
 B2A_DEFINE_ERROR_READER(prefill_d64)

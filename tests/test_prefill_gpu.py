@@ -185,3 +185,32 @@ def test_causal_needs_nk_at_least_n(b2a):
     k = torch.zeros(1, 1, 64, 64, dtype=torch.float16, device="cuda")
     with pytest.raises(RuntimeError, match="Nk >= N"):
         b2a.forward(q, k, k, causal=True)
+
+
+# Non-causal D = 64 launches whose plain grid would fill less than the GPU run
+# split-KV: a cluster of 2-8 CTAs shares each 256-row block, one slice of the
+# KV tiles each, merged in-kernel.  The split factor a 148-SM B200 picks is
+# noted for each case; the parity bar is the same as for the unsplit kernel.
+SPLIT_CASES = [
+    # B, H, Hkv, N, Nk, dtype
+    (1, 1, 1, 256, 1024, torch.float16),    # 1 block, 8 KV tiles: 8 splits of one tile
+    (1, 4, 4, 1000, 1000, torch.bfloat16),  # 16 blocks (the last ragged): 8 splits
+    (1, 2, 2, 300, 700, torch.float16),     # 4 blocks, 6 tiles: 2 splits of 3
+    (1, 2, 1, 200, 130, torch.bfloat16),    # GQA; split 2 holds one tile of only 2 keys
+    (2, 4, 2, 1024, 3000, torch.float16),   # 32 blocks, 24 tiles: 4 splits of 6
+]
+
+
+@pytest.mark.parametrize("B,H,Hkv,N,Nk,dt", SPLIT_CASES, ids=lambda x: str(x))
+def test_split_kv_d64(b2a, B, H, Hkv, N, Nk, dt):
+    q, _, _ = seeded((B, H, N, 64), (B, Hkv, N, 64), 600 + N, 1.0, dt)
+    k = dev(ora.seeded_normal((B, Hkv, Nk, 64), 700 + Nk), dt)
+    v = dev(ora.seeded_normal((B, Hkv, Nk, 64), 800 + Nk), dt)
+    b2a.device_error_flags()
+    O, L = b2a.forward(q, k, v)
+    Or, Lr = ora.naive_attention(host(q), host(k), host(v))
+    name = "bfloat16" if dt == torch.bfloat16 else "float16"
+    assert_parity(O, L, Or, Lr, name, 1.0, f"split-KV N={N} Nk={Nk}")
+    assert torch.equal(b2a.forward_only(q, k, v), O)
+    torch.cuda.synchronize()
+    assert b2a.device_error_flags() == 0
