@@ -335,34 +335,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(BAR_EPI(t));
     if (ok) ok = mbar_wait(BAR_EPI(t), 0, abort_flag);
+    float a[32], b[32];
+    float M = -INFINITY, Lsum = 0.f, f0 = 0.f, f1 = 0.f;
     if (ok) {
       tc_fence_after();
       const float2 ml0 = s_ml[(t * 2 + 0) * 128 + row];
       const float2 ml1 = s_ml[(t * 2 + 1) * 128 + row];
-      const float M = fmaxf(ml0.x, ml1.x);
+      M = fmaxf(ml0.x, ml1.x);
       const float w0 = (ml0.x == -INFINITY) ? 0.f : ex2_mufu(ml0.x - M);
       const float w1 = (ml1.x == -INFINITY) ? 0.f : ex2_mufu(ml1.x - M);
-      const float Lsum = ml0.y * w0 + ml1.y * w1;
+      Lsum = ml0.y * w0 + ml1.y * w1;
       const float inv = 1.f / Lsum;
-      const float f0 = w0 * inv, f1 = w1 * inv;
+      f0 = w0 * inv;
+      f1 = w1 * inv;
       const uint32_t o0 = tmem + lane_base + 256 + 64 * (2 * t) + 32 * h;
       const uint32_t o1 = tmem + lane_base + 256 + 64 * (2 * t + 1) + 32 * h;
-      float a[32], b[32];
       tmem_ld32(o0, a);
       tmem_ld32(o1, b);
       tmem_ld_wait();
-      if constexpr (SPLIT) {
-        // this CTA's partial for the row: O normalised by its own sum, and (M, L)
-        // (the K/V ring is free once both Q tiles' products have run)
-        ok = mbar_wait(BAR_PVD(1 - t), (nkv_t[1 - t] - 1) & 1, abort_flag);
-        float* po = reinterpret_cast<float*>(sp + kOffPartO) + (t * BM + row) * kPartStride + 32 * h;
-#pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          *reinterpret_cast<float4*>(po + i) =
-              make_float4(a[i] * f0 + b[i] * f1, a[i + 1] * f0 + b[i + 1] * f1,
-                          a[i + 2] * f0 + b[i + 2] * f1, a[i + 3] * f0 + b[i + 3] * f1);
-        if (h == 0) reinterpret_cast<float2*>(sp + kOffPartML)[t * BM + row] = make_float2(M, Lsum);
-      } else if (grow < N) {
+      if (!SPLIT && grow < N) {
         typename E::T* orow =
             reinterpret_cast<typename E::T*>(out) + ((size_t)bh * N + grow) * D + 32 * h;
 #pragma unroll
@@ -379,6 +370,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if constexpr (SPLIT) {
+      // This CTA's partial for the row: O normalised by its own sum, and (M, L),
+      // written over the K/V ring once no UMMA reads it.  Every softmax thread
+      // has waited for its own tile's last PV above (that barrier is at most one
+      // phase behind; a wait on the other tile's barrier could match an older
+      // phase of the same parity and return early); the named barrier, reached
+      // by all softmax threads on every path, extends that to both tiles.
+      tc_fence_before();
+      named_barrier_sync(1, kSoftmaxWGs * 128);
+      if (ok) {
+        float* po = reinterpret_cast<float*>(sp + kOffPartO) + (t * BM + row) * kPartStride + 32 * h;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(po + i) =
+              make_float4(a[i] * f0 + b[i] * f1, a[i + 1] * f0 + b[i + 1] * f1,
+                          a[i + 2] * f0 + b[i + 2] * f1, a[i + 3] * f0 + b[i + 3] * f1);
+        if (h == 0) reinterpret_cast<float2*>(sp + kOffPartML)[t * BM + row] = make_float2(M, Lsum);
+      }
       // merge the cluster's partials, this CTA taking rows [crank * rows_per, ...):
       //   M* = max_c M_c, W_c = L_c 2^(M_c - M*), O = sum_c W_c O_c / sum_c W_c,
       //   L = M* ln 2 + ln sum_c W_c

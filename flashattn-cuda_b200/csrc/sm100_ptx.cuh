@@ -239,6 +239,11 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Named barrier `id` (1..15) over `nthreads` threads of the CTA (whole warps).
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // thread-block clusters: rank, cluster-wide barrier, distributed shared memory
 // ---------------------------------------------------------------------------
