@@ -69,8 +69,9 @@ constexpr uint32_t kOffPartML = kOffPartO + kRowsPerCta * kPartStride * 4;
 static_assert(kOffPartML + kRowsPerCta * 8 <= kOffML, "split partials must fit in the K/V ring");
 constexpr int kMaxSplits = 8;
 
-// SPLIT (non-causal only): a cluster of `splits` CTAs along x shares one
-// 256-row block; CTA rank r takes KV tiles [r * kv_per_split, ...) and the
+// SPLIT: a cluster of `splits` CTAs along x shares one 256-row block; CTA
+// rank r takes KV tiles [r * kv_per_split, ...) of those the block sees (under
+// a causal mask possibly none) and the
 // partial results are merged through distributed shared memory at the end
 // (the LSE-weighted combine of the split-KV decode, done in-kernel).
 template <bool BF16, bool CAUSAL, bool SPLIT>
@@ -80,7 +81,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap tmV, void* __restrict__ out,
                        float* __restrict__ lse, int N, int Nk, int H, int group, float scale_log2,
                        int splits, int kv_per_split) {
-  static_assert(!(SPLIT && CAUSAL), "the split-KV form is non-causal");
   using E = Elem<BF16>;
   constexpr int S = kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -114,13 +114,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   // this CTA's KV tiles: kv_base + [0, nkv_t[t]) for Q tile t (every loop below
   // runs over the local index j; kv_base + j is the tile's place in the sequence)
   const int kv_base = SPLIT ? (int)crank * kv_per_split : 0;
+  // (split: a causal rank whose slice lies past the block's last visible key
+  // has no tile at all and contributes an empty partial)
   int nkv_t[2];
 #pragma unroll
-  for (int t = 0; t < 2; ++t)
-    nkv_t[t] = SPLIT ? min(kv_per_split, nkv_all - kv_base)
-               : CAUSAL ? min(nkv_all, (q0 + (t + 1) * BM + koff + BN - 1) / BN)
-                        : nkv_all;
-  const int nkv = nkv_t[1];
+  for (int t = 0; t < 2; ++t) {
+    nkv_t[t] = CAUSAL ? min(nkv_all, (q0 + (t + 1) * BM + koff + BN - 1) / BN) : nkv_all;
+    if (SPLIT) nkv_t[t] = max(0, min(kv_per_split, nkv_t[t] - kv_base));
+  }
+  const int nkv = nkv_t[1];  // >= nkv_t[0]
 
   if (warp == kProducerWarp && lane == 0) {
     for (int i = 0; i < kNumBars; ++i) {
@@ -148,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp >= 16) {
     setmaxnreg_dec<kRegsCtrl>();
-    if (warp == kProducerWarp && lane == 0) {
+    if (warp == kProducerWarp && lane == 0 && nkv > 0) {
       // ---------------------------------------------------------- producer
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -189,13 +191,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < HALF / 16; ++kk)
           umma_f16_ts(d_o, a_p + kk * 8, vd + kk * 128, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(BAR_Q, 0, abort_flag) && mbar_wait(BAR_KF(0), 0, abort_flag);
+      bool ok = nkv > 0 && mbar_wait(BAR_Q, 0, abort_flag) && mbar_wait(BAR_KF(0), 0, abort_flag);
       if (ok) {
         tc_fence_after();
-        issue_s(0, 0);
-        umma_commit(BAR_SF(0));
-        issue_s(1, 0);
-        umma_commit(BAR_SF(1));
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (nkv_t[t] == 0) continue;  // split-KV: no tile of this slice is visible
+          issue_s(t, 0);
+          umma_commit(BAR_SF(t));
+        }
       }
       for (int j = 0; ok && j < nkv; ++j) {
         const int st = j % S;
@@ -330,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // exchange (m, l) with the other half of the row, then merge:
     //   M = max(m0, m1), w_i = 2^(m_i - M), L = l0 w0 + l1 w1,
     //   O = (w0 O_{t,0} + w1 O_{t,1}) / L   (this thread: columns [32h, 32h+32))
-    if (ok) ok = mbar_wait(BAR_PVD(t), (my_nkv - 1) & 1, abort_flag);
+    if (ok && my_nkv > 0) ok = mbar_wait(BAR_PVD(t), (my_nkv - 1) & 1, abort_flag);
     s_ml[(t * 2 + h) * 128 + row] = make_float2(ok ? m_run : -INFINITY, ok ? l_run : 0.f);
     __syncwarp();
     if (lane == 0) mbar_arrive(BAR_EPI(t));
@@ -350,9 +354,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       f1 = w1 * inv;
       const uint32_t o0 = tmem + lane_base + 256 + 64 * (2 * t) + 32 * h;
       const uint32_t o1 = tmem + lane_base + 256 + 64 * (2 * t + 1) + 32 * h;
-      tmem_ld32(o0, a);
-      tmem_ld32(o1, b);
-      tmem_ld_wait();
+      if (my_nkv > 0) {  // warp-uniform: tile t's count
+        tmem_ld32(o0, a);
+        tmem_ld32(o1, b);
+        tmem_ld_wait();
+      }
       if (!SPLIT && grow < N) {
         typename E::T* orow =
             reinterpret_cast<typename E::T*>(out) + ((size_t)bh * N + grow) * D + 32 * h;
@@ -378,14 +384,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       // by all softmax threads on every path, extends that to both tiles.
       tc_fence_before();
       named_barrier_sync(1, kSoftmaxWGs * 128);
-      if (ok) {
+      {
+        // (-inf, 0, O = 0) where this rank's slice shows the row no key
+        const bool seen = ok && my_nkv > 0 && M != -INFINITY;
         float* po = reinterpret_cast<float*>(sp + kOffPartO) + (t * BM + row) * kPartStride + 32 * h;
 #pragma unroll
         for (int i = 0; i < 32; i += 4)
           *reinterpret_cast<float4*>(po + i) =
-              make_float4(a[i] * f0 + b[i] * f1, a[i + 1] * f0 + b[i + 1] * f1,
-                          a[i + 2] * f0 + b[i + 2] * f1, a[i + 3] * f0 + b[i + 3] * f1);
-        if (h == 0) reinterpret_cast<float2*>(sp + kOffPartML)[t * BM + row] = make_float2(M, Lsum);
+              seen ? make_float4(a[i] * f0 + b[i] * f1, a[i + 1] * f0 + b[i + 1] * f1,
+                                 a[i + 2] * f0 + b[i + 2] * f1, a[i + 3] * f0 + b[i + 3] * f1)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (h == 0)
+          reinterpret_cast<float2*>(sp + kOffPartML)[t * BM + row] =
+              seen ? make_float2(M, Lsum) : make_float2(-INFINITY, 0.f);
       }
       // merge the cluster's partials, this CTA taking rows [crank * rows_per, ...):
       //   M* = max_c M_c, W_c = L_c 2^(M_c - M*), O = sum_c W_c O_c / sum_c W_c,
@@ -404,7 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int c = 0; c < splits; ++c) {
           const float2 ml = ld_dsmem_f2(mapa_shared(pml_base + r * 8, (uint32_t)c));
-          const float w = (ml.x == -INFINITY) ? 0.f : ml.y * ex2_mufu(ml.x - mx);
+          if (ml.x == -INFINITY) continue;  // an empty partial
+          const float w = ml.y * ex2_mufu(ml.x - mx);
           const float4 o =
               ld_dsmem_f4(mapa_shared(po_base + (r * kPartStride + c4) * 4, (uint32_t)c));
           lt += w;
@@ -492,9 +504,9 @@ static int launch_prefill_d64(const void* q, const void* k, const void* v, void*
   return B2A_OK;
 }
 
-// Split-KV factor for a non-causal launch: the largest power of two <= 8 whose
-// clusters still fit in one wave on the device's SMs and give every split at
-// least one KV tile; 1 (no split) when the plain grid already fills the GPU.
+// Split-KV factor: the largest power of two <= 8 whose clusters still fit in
+// one wave on the device's SMs and give every rank at least one KV tile of the
+// heaviest block; 1 (no split) when the plain grid already fills the GPU.
 static int d64_splits(int B, int H, int N, int Nk) {
   static int sms[kMaxDevices] = {};
   int dev = 0;
@@ -516,7 +528,7 @@ int prefill_d64_dispatch(const void* q, const void* k, const void* v, void* o, f
                          int H, int Hkv, int N, int Nk, int dtype, int causal, float scale,
                          cudaStream_t stream) {
   const bool bf = dtype == B2A_BF16;
-  const int splits = causal ? 1 : d64_splits(B, H, N, Nk);
+  const int splits = d64_splits(B, H, N, Nk);
 #define B2A_D64(BB, CC, SS)                                                                      \
   if (bf == BB && (causal != 0) == CC && (splits > 1) == SS)                                    \
     return launch_prefill_d64<BB, CC, SS>(q, k, v, o, lse, B, H, Hkv, N, Nk, scale, splits,   \
@@ -527,6 +539,8 @@ int prefill_d64_dispatch(const void* q, const void* k, const void* v, void* o, f
   B2A_D64(true, false, false)
   B2A_D64(true, false, true)
   B2A_D64(true, true, false)
+  B2A_D64(false, true, true)
+  B2A_D64(true, true, true)
 #undef B2A_D64
   return set_error(B2A_ERR_UNSUPPORTED, "prefill d64: no kernel for this configuration");
 }

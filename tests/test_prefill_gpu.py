@@ -214,3 +214,29 @@ def test_split_kv_d64(b2a, B, H, Hkv, N, Nk, dt):
     assert torch.equal(b2a.forward_only(q, k, v), O)
     torch.cuda.synchronize()
     assert b2a.device_error_flags() == 0
+
+
+# Causal D = 64 launches split too; ranks whose KV slice lies past a block's
+# last visible key have no tile and contribute an empty partial.
+SPLIT_CAUSAL_64 = [
+    # B, H, Hkv, N, Nk, dtype
+    (1, 1, 1, 1024, 1024, torch.float16),   # 4 blocks x 8 ranks; block 0 uses 2 of 8
+    (1, 2, 2, 300, 300, torch.bfloat16),    # 4 blocks x 2 ranks, rank 1 of block 0 empty
+    (1, 4, 2, 640, 640, torch.float16),     # 12 blocks x 2 ranks; a rank with tile 1 only
+    (1, 1, 1, 129, 4096, torch.bfloat16),   # one block x 8 ranks, causal offset 3967
+]
+
+
+@pytest.mark.parametrize("B,H,Hkv,N,Nk,dt", SPLIT_CAUSAL_64, ids=lambda x: str(x))
+def test_split_kv_d64_causal(b2a, B, H, Hkv, N, Nk, dt):
+    q, _, _ = seeded((B, H, N, 64), (B, Hkv, N, 64), 1200 + N, 1.0, dt)
+    k = dev(ora.seeded_normal((B, Hkv, Nk, 64), 1300 + Nk), dt)
+    v = dev(ora.seeded_normal((B, Hkv, Nk, 64), 1400 + Nk), dt)
+    b2a.device_error_flags()
+    O, L = b2a.forward(q, k, v, causal=True)
+    Or, Lr = ora.naive_attention(host(q), host(k), host(v), causal=True)
+    name = "bfloat16" if dt == torch.bfloat16 else "float16"
+    assert_parity(O, L, Or, Lr, name, 1.0, f"causal split-KV N={N} Nk={Nk}")
+    assert torch.equal(b2a.forward_only(q, k, v, causal=True), O)
+    torch.cuda.synchronize()
+    assert b2a.device_error_flags() == 0
