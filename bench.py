@@ -1,16 +1,21 @@
 #!/usr/bin/env python
 """Benchmark of the b200attn hot path (driver contract: one JSON line on rank 0).
 
-Default workload: BASELINE config 2, the reference's headline shape -- non-causal
-prefill forward, B=1, H=8, N=4096, D=64, fp16, returning O and L
-(bench/bench_fa3_headline.py of the reference times the same call, forward()+L).
-A step is one forward over one batch.  Other configs: --config 1|2|3|3s|4|4s|5a|5b.
+Default workload: config 3 -- causal prefill forward, B=4, H=32, N=8192,
+D=128, bf16, returning O and L: the shape the "% of BF16 tensor peak" target
+is stated on.  Its 128 (b, h) units shard across torchrun ranks with no
+collective.  The same line carries a `secondary` object with config 2 (the
+reference's headline shape, B=1 H=8 N=4096 D=64 fp16 non-causal, which
+bench/bench_fa3_headline.py of the reference times as forward()+L) and config 4
+(split-KV GQA decode), timed in the same process.  A step is one forward over
+one batch.  Other main configs: --config 1|2|3s|4|4s|5a|5b|6|6s|7|7s|7m.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
 
 Multi-GPU (torchrun, one rank per GPU): configs 1/2 run independent replicas
 (weak scaling); config 3 shards its 128 (b, h) units and configs 4/5a shard
-batch rows across ranks with no collective (strong scaling).  Time is device
+batch rows across ranks with no collective (strong scaling); config 5b shards
+the KV sequence and all-gathers the partials over NCCL.  Time is device
 time over the K timed steps (CUDA events on the launching stream), max over
 ranks.  Inputs: seeded synthetic data of the configs' shapes; steps rotate over
 enough input sets that the bytes touched between reuses exceed the 126 MB L2.
@@ -29,6 +34,7 @@ import subprocess
 import sys
 import tempfile
 import time
+from types import SimpleNamespace
 
 import numpy as np
 
@@ -238,19 +244,16 @@ def cpu_sample(cfg_key: str, steps: int, warmup: int):
 
 
 # ------------------------------------------------------------------ GPU arm
-def run_ours(args, rank, world, local_rank):
+def make_workload(cfg_key, args, rank, world, dev):
+    """Device-resident inputs and the step function of one workload on this rank
+    (plus the host buffers and call of its end-to-end form)."""
     import torch
-    import torch.distributed as dist
     import b200attn
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    c = CONFIGS[args.config]
+    c = CONFIGS[cfg_key]
     tdt = torch.float16 if c["dtype"] == "float16" else torch.bfloat16
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-    stream = torch.cuda.current_stream(dev)
 
-    # ---- build the per-rank workload and one step function (device-resident inputs)
     if c["kind"] == "prefill":
         units = c["B"] * c["H"]
         B = c["B"]
@@ -507,6 +510,119 @@ def run_ours(args, rank, world, local_rank):
         workload = dict(workload=c["name"], B=B, total_tokens=int(lens.sum()),
                         pages=P, pages_per_split=c["pps"], dtype=c["dtype"])
 
+    return SimpleNamespace(c=c, step=step, nsets=nsets, work_per_step=work_per_step,
+                           unit=unit, kernel_regex=kernel_regex, bound=bound, h2d=h2d,
+                           d2h=d2h, e2e_in=e2e_in, host_out=host_out,
+                           static_out=static_out, e2e_run=e2e_run, workload=workload)
+
+
+def roofline_of(w, cfg_key, kernel_ms, clocks, peaks) -> dict:
+    """Roofline object of a workload: algorithmic work per step over the median
+    per-step device time, against the measured peak of its bound."""
+    scale = 1e12 if w.unit == "TFLOP/s" else 1e9
+    achieved = w.work_per_step / (kernel_ms / 1e3) / scale
+    if w.bound == "tensor":
+        # the burst GEMM figure for a kernel running at full clock, the sustained
+        # one when the timed region ran under the power cap
+        capped = "sw_power_cap" in clocks.get("reasons", []) or (
+            clocks.get("sm_mhz") and clocks.get("sm_max_mhz")
+            and clocks["sm_mhz"] < 0.9 * clocks["sm_max_mhz"])
+        sustained = capped and peaks.get("bf16_tflops_sustained")
+        pk = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+        peak_kind = " (sustained)" if sustained else " (burst)"
+        runit = "TFLOP/s"
+    else:
+        pk = peaks["hbm_gbs"]
+        peak_kind = ""
+        runit = "GB/s"
+    return {"bound": w.bound, "achieved": round(achieved, 2), "peak": pk, "unit": runit,
+            "frac": round(achieved / pk, 4), "traffic": read_traffic(f"config{cfg_key}"),
+            "traffic_source": "profiles/traffic.json: dram__bytes_read.sum + "
+                              "dram__bytes_write.sum of one ncu capture, bytes per launch "
+                              "(a stored figure, not measured by this run)",
+            "peak_source": peaks["source"] + peak_kind,
+            "kernel": w.kernel_regex, "launch_ms_median": round(kernel_ms, 5),
+            "note": "achieved = algorithmic work per step / median per-step device time "
+                    "(CUDA events on the launching stream, steps queued behind a GPU sleep so "
+                    "that host launch gaps are not counted)"}
+
+
+def kernel_step_times(torch, step, stream, first: int, n: int) -> list:
+    """Device time of each of n steps, CUDA events around each on `stream`.  The
+    launches queue behind a GPU-side sleep first, so the events measure the GPU
+    work of a step and not the host's launch gaps."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n)]
+    torch.cuda._sleep(int(min(n, 200) * 40e-6 * 2e9))   # ~40 us of host time per step
+    for i in range(n):
+        evs[i][0].record(stream)
+        step(first + i)
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+SECONDARY = ("2", "4")
+
+
+def run_secondary(args, rank, world, dev, clocks, peaks) -> dict:
+    """Value and roofline of the other headline workloads (config 2, the
+    reference's own headline shape, and config 4, split-KV decode), timed in the
+    same process on the same box: warm-up, then K device-timed steps (max over
+    ranks), then the per-step kernel time for the roofline."""
+    import torch
+    import torch.distributed as dist
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+    for key in SECONDARY:
+        if key == args.config:
+            continue
+        w = make_workload(key, args, rank, world, dev)
+        steps = 50 if w.c["kind"] == "prefill" else 20
+        for i in range(max(args.warmup, 3)):
+            w.step(i)
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            w.step(i)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t[0])
+        kms = statistics.median(kernel_step_times(torch, w.step, stream, 0, steps))
+        scale = 1e12 if w.unit == "TFLOP/s" else 1e9
+        out[f"config{key}"] = {
+            "workload": w.workload["workload"],
+            "value": round(w.work_per_step * steps * world / (ms / 1e3) / scale, 3),
+            "unit": w.unit, "steps": steps, "ms_per_step": round(ms / steps, 5),
+            "scaling": "weak" if not w.c["shard"] else "strong",
+            "l2": f"{w.nsets} rotating input sets" if w.nsets > 1 else "inputs larger than L2",
+            "roofline": roofline_of(w, key, kms, clocks, peaks)}
+        del w
+        torch.cuda.empty_cache()
+    return out
+
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(dev)
+    w = make_workload(args.config, args, rank, world, dev)
+    c, step, nsets, work_per_step, unit = w.c, w.step, w.nsets, w.work_per_step, w.unit
+    kernel_regex, bound, h2d, d2h = w.kernel_regex, w.bound, w.h2d, w.d2h
+    e2e_in, host_out, static_out, e2e_run = w.e2e_in, w.host_out, w.static_out, w.e2e_run
+    workload = w.workload
+
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local_rank])
@@ -558,14 +674,7 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- per-step device time of the dominant kernel(s), for the roofline: a
     # separate pass, because events between steps add a few microseconds each
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    for i in range(args.steps):
-        kev[i][0].record(stream)
-        step(args.warmup + i)
-        kev[i][1].record(stream)
-    torch.cuda.synchronize(dev)
-    step_ms = [a.elapsed_time(b) for a, b in kev]
+    step_ms = kernel_step_times(torch, step, stream, args.warmup, args.steps)
 
     # ---- end-to-end through the public API with host buffers.  Every step copies
     # its inputs host->device and its outputs device->host inside the timed
@@ -627,27 +736,11 @@ def run_ours(args, rank, world, local_rank):
 
     peaks = read_peaks()
     kernel_ms = statistics.median(step_ms)
-    achieved = work_per_step / (kernel_ms / 1e3) / scale
-    if bound == "tensor":
-        # the burst GEMM figure for a kernel running at full clock, the sustained
-        # one when the timed region ran under the power cap
-        capped = "sw_power_cap" in clocks.get("reasons", []) or (
-            clocks.get("sm_mhz") and clocks.get("sm_max_mhz")
-            and clocks["sm_mhz"] < 0.9 * clocks["sm_max_mhz"])
-        sustained = capped and peaks.get("bf16_tflops_sustained")
-        pk = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
-        peak_kind = " (sustained)" if sustained else " (burst)"
-        runit = "TFLOP/s"
-    else:
-        pk = peaks["hbm_gbs"]
-        peak_kind = ""
-        runit = "GB/s"
-    roofline = {"bound": bound, "achieved": round(achieved, 2), "peak": pk, "unit": runit,
-                "frac": round(achieved / pk, 4), "traffic": read_traffic(f"config{args.config}"),
-                "peak_source": peaks["source"] + peak_kind,
-                "kernel": kernel_regex, "launch_ms_median": round(kernel_ms, 5),
-                "note": "achieved = algorithmic work per step / median per-step device time "
-                        "(CUDA events on the launching stream)"}
+    roofline = roofline_of(w, args.config, kernel_ms, clocks, peaks)
+
+    secondary = None
+    if not args.no_secondary:
+        secondary = run_secondary(args, rank, world, dev, clocks, peaks)
 
     out = None
     if rank == 0:
@@ -681,6 +774,7 @@ def run_ours(args, rank, world, local_rank):
             "roofline": roofline,
             "cpu_baseline": cpu,
             "gpu_launches": kernel_launches,
+            "secondary": secondary,
             "clocks": clocks,
         }
     return out
@@ -718,9 +812,11 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="3", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the config 2 / config 4 lines timed after the main workload")
     ap.add_argument("--graph", action="store_true",
                     help="decode configs: replay each step as one captured CUDA graph")
     args = ap.parse_args()

@@ -11,6 +11,7 @@ import os
 _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libb200attn.so")
 
 B2A_OK = 0
+B2A_ERR_TIMEOUT = 5
 B2A_F16 = 0
 B2A_BF16 = 1
 
@@ -42,6 +43,7 @@ _SIGNATURES = {
     "b2a_backward": (_c_int, [_vp] * 10 + [_c_int] * 8 + [_c_float, _vp]),
     "b2a_backward_workspace_floats": (ctypes.c_int64, [_c_int] * 4),
     "b2a_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint32)]),
+    "b2a_selftest_wait_timeout": (_c_int, [_c_int, _vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

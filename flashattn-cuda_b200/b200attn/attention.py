@@ -346,12 +346,28 @@ def decode_paged(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
 
 
 def device_error_flags() -> int:
-    """Read and clear the current device's kernel error word (synchronises)."""
+    """Read and clear the current device's kernel error word (synchronises).
+
+    Bit 0 means a bounded device-side wait timed out; the library reports that
+    as B2A_ERR_TIMEOUT, which this function returns as the flag value rather
+    than raising (use `check_device()` to raise on it)."""
     import ctypes
     lib = _lib.load()
     v = ctypes.c_uint32(0)
-    _lib.check(lib.b2a_device_error(ctypes.byref(v)))
+    rc = lib.b2a_device_error(ctypes.byref(v))
+    if rc != _lib.B2A_ERR_TIMEOUT:
+        _lib.check(rc)
     return int(v.value)
+
+
+def check_device() -> None:
+    """Raise RuntimeError when a kernel since the last check reported an error
+    (a timed-out wait, a bad block-table entry, ...); clears the word."""
+    flags = device_error_flags()
+    if flags:
+        raise RuntimeError(f"b200attn: device error word 0x{flags:x} (bit 0: a wait timed out; "
+                           "bit 1: bad block-table entry; bit 2: no page for an appended token; "
+                           "bit 3: bad cu_seqlens / sequence longer than max_seqlen_q)")
 
 
 def default_scale(D: int) -> float:

@@ -33,12 +33,17 @@ int make_tmap_tokens(CUtensorMap* map, const void* base, CUtensorMapDataType dt,
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner,
                  uint64_t rows, uint32_t box_inner, uint32_t box_rows, bool swizzle128);
 
+// B2A_OK when an sm_100 device is current and dtype is f16/bf16; otherwise
+// B2A_ERR_NO_DEVICE / B2A_ERR_UNSUPPORTED with the message recorded.
+int require_device(int dtype);
+
 // Read-and-clear of each translation unit's device error word.
 int take_error_flags_prefill(uint32_t* flags);
 int take_error_flags_prefill_d64(uint32_t* flags);
 int take_error_flags_kvcache(uint32_t* flags);
 int take_error_flags_backward(uint32_t* flags);
 int take_error_flags_decode(uint32_t* flags);
+int take_error_flags_selftest(uint32_t* flags);
 
 // Defines take_error_flags_<unit>() for the unit that expands it.
 #define B2A_DEFINE_ERROR_READER(unit)                                          \

@@ -98,6 +98,8 @@ int set_error(int status, const char* msg) {
   return status;
 }
 
+int require_device(int dtype) { return common_checks(dtype); }
+
 int set_cuda_error(cudaError_t e, const char* what) {
   snprintf(t_last_error, sizeof t_last_error, "%s: %s", what, cudaGetErrorString(e));
   return B2A_ERR_CUDA;
@@ -416,7 +418,15 @@ int b2a_device_error(uint32_t* flags) {
   B2A_TRY(take_error_flags_kvcache(&v));
   B2A_TRY(take_error_flags_backward(&v));
   B2A_TRY(take_error_flags_decode(&v));
+  B2A_TRY(take_error_flags_selftest(&v));
   *flags = v;
+  if (v & 1u) {
+    char buf[160];
+    snprintf(buf, sizeof buf,
+             "a device-side bounded wait timed out (error word 0x%x); outputs of the calls "
+             "since the last check are undefined", v);
+    return set_error(B2A_ERR_TIMEOUT, buf);
+  }
   return B2A_OK;
 }
 

@@ -124,7 +124,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int hkv = blockIdx.y;
   const int b = blockIdx.z;
 
-  const int len = PAGED ? kv_lens[b] : Lkv;
+  int len = PAGED ? kv_lens[b] : Lkv;
+  if (PAGED && (len < 0 || len > max_pages * page_size)) {
+    // a length the block table cannot hold: flag it and keep to the table
+    if (split == 0 && hkv == 0 && threadIdx.x == 0) atomicOr(&g_error_flags, 2u);
+    len = min(max(len, 0), max_pages * page_size);
+  }
   const int t_begin = split * tps;
   const int t_end = min(len, t_begin + tps);
   const int head0 = b * H + hkv * G;  // first query head (flattened b*H + h)
@@ -359,7 +364,7 @@ __global__ void combine_kernel(const float* __restrict__ o_part, const float* __
   using T = typename Elem<BF16>::T;
   const int bh = blockIdx.x;
   int ns = S;
-  if (kv_lens != nullptr) ns = min(S, (kv_lens[bh / H] + tps - 1) / tps);
+  if (kv_lens != nullptr) ns = max(0, min(S, (kv_lens[bh / H] + tps - 1) / tps));
   const float* lp = l_part + (size_t)bh * S;
   float M = -INFINITY;
   for (int s = 0; s < ns; ++s) M = fmaxf(M, lp[s]);
@@ -370,8 +375,10 @@ __global__ void combine_kernel(const float* __restrict__ o_part, const float* __
     sum += w;
     if (d < D) acc += w * o_part[((size_t)bh * S + s) * D + d];
   }
-  if (d < D) reinterpret_cast<T*>(out)[(size_t)bh * D + d] = Elem<BF16>::from(acc / sum);
-  if (lse != nullptr && d == 0) lse[bh] = M + logf(sum);
+  // no key at all (an empty sequence): O = 0, L = -inf
+  if (d < D)
+    reinterpret_cast<T*>(out)[(size_t)bh * D + d] = Elem<BF16>::from(sum > 0.f ? acc / sum : 0.f);
+  if (lse != nullptr && d == 0) lse[bh] = sum > 0.f ? M + logf(sum) : -INFINITY;
 }
 
 }  // namespace decode
@@ -504,6 +511,10 @@ extern "C" int b2a_decode_paged_noalloc(const void* q, const void* k_pool, const
                                         int pages_per_split, int dtype, float scale,
                                         void* stream) {
   using namespace b2a;
+  // the device check comes first: the scratch address exists only on a
+  // device that can run the kernels
+  int rc = require_device(dtype);
+  if (rc != B2A_OK) return rc;
   if (B <= 0 || H <= 0 || D <= 0 || max_pages <= 0 || pages_per_split <= 0)
     return set_error(B2A_ERR_INVALID_ARG,
                      "B, H, D, max_pages and pages_per_split must be > 0");
@@ -520,7 +531,7 @@ extern "C" int b2a_decode_paged_noalloc(const void* q, const void* k_pool, const
     return set_error(B2A_ERR_INVALID_ARG, buf);
   }
   float* scratch = nullptr;
-  int rc = noalloc_scratch_ptr(&scratch);
+  rc = noalloc_scratch_ptr(&scratch);
   if (rc != B2A_OK) return rc;
   float* o_part = scratch;                       // [B, H, splits, D]
   float* l_part = scratch + rows * (size_t)D;    // [B, H, splits]; 16-byte aligned (D % 4 == 0)

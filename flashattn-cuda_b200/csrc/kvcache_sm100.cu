@@ -31,9 +31,12 @@ __global__ void __launch_bounds__(kThreads)
   const int t = blockIdx.x * ROWS + threadIdx.x / VPR;
   const int vec = threadIdx.x % VPR;
   if (t >= T) return;
-  const int pos = kv_lens[b] + t;
-  const int pidx = pos / page_size;
-  int page = pidx < max_pages ? block_table[(size_t)b * max_pages + pidx] : -1;
+  // 64-bit position: kv_lens[b] + t must not wrap; a negative or too large
+  // position has no block-table entry
+  const long long pos64 = (long long)kv_lens[b] + t;
+  const long long pidx64 = pos64 >= 0 ? pos64 / page_size : -1;
+  int page = (pidx64 >= 0 && pidx64 < max_pages) ? block_table[(size_t)b * max_pages + pidx64] : -1;
+  const int pos = (int)pos64;
   if (page < 0 || page >= num_pages) {
     atomicOr(&g_error_flags, 4u);  // no page assigned for this position: token dropped
     return;

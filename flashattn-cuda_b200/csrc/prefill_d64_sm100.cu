@@ -427,14 +427,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int qrow = q0 + r;
         if (qrow < N) {
-          const float inv = 1.f / lt;
+          // lt == 0 only when every rank aborted on a timed-out wait (error
+          // bit 0 is set then): O = 0, L = -inf instead of inf / NaN
+          const float inv = lt > 0.f ? 1.f / lt : 0.f;
           uint2 wv;
           wv.x = pack2_u32<BF16>(acc.x * inv, acc.y * inv);
           wv.y = pack2_u32<BF16>(acc.z * inv, acc.w * inv);
           *reinterpret_cast<uint2*>(reinterpret_cast<typename E::T*>(out) +
                                     ((size_t)bh * N + qrow) * D + c4) = wv;
           if (c4 == 0 && lse != nullptr)
-            lse[(size_t)bh * N + qrow] = mx * 0.69314718055994531f + logf(lt);
+            lse[(size_t)bh * N + qrow] =
+                lt > 0.f ? mx * 0.69314718055994531f + logf(lt) : -INFINITY;
         }
       }
       cluster_sync_all();  // no CTA leaves while a peer still reads its partials

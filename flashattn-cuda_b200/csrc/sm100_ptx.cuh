@@ -73,14 +73,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // limit ran out (the caller must then stop using the pipeline); the error is
 // recorded in g_error_flags and in *abort (a shared-memory flag every role
 // polls so that the whole CTA winds down).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+// `limit_ns` is the give-up time (kWaitLimitNs for the kernels' pipelines).
+__device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity,
+                                                volatile int* abort, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++spins & 255u) == 0u) {
       if (*abort) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit_ns) {
         atomicOr(&g_error_flags, kErrWaitTimeout);
         *abort = 1;
         return false;
@@ -88,6 +90,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
   }
   return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  return mbar_wait_limit(bar, parity, abort, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------------------
@@ -363,10 +368,10 @@ __device__ __forceinline__ float ex2_mufu(float x) {
 // 2^x for a pair of x <= ~64 on the FMA/ALU pipes, so that part of a softmax's
 // exponentials can run beside the MUFU unit.  Method: Cody-Waite style range
 // reduction x = n + f with n = round(x) obtained by adding and subtracting
-// 1.5 * 2^23 (f in [-1/2, 1/2]); 2^f by a degree-4 polynomial whose
-// coefficients were fitted here to 2^f on [-1/2, 1/2] in relative error
-// (Chebyshev nodes, iteratively reweighted least squares toward equiripple;
-// max relative error 2.6e-6); 2^n applied by adding n to the exponent field.
+// 1.5 * 2^23 (f in [-1/2, 1/2]); 2^f by a degree-4 polynomial fitted to 2^f
+// on [-1/2, 1/2] in relative error by exp2_poly_fit.py (next to this file:
+// Chebyshev nodes, Lawson's reweighted least squares toward equiripple; max
+// relative error 2.6e-6); 2^n applied by adding n to the exponent field.
 // Inputs below -126 are clamped to -126 (result ~1e-38, never a NaN).
 __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   const float2 kShift = make_float2(12582912.f, 12582912.f);

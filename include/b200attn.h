@@ -185,7 +185,9 @@ int b2a_kv_append_paged(const void* k_new, const void* v_new, void* k_pool,
  * last call's contents (nothing in it has to start at zero: every entry a
  * call reads is written earlier in the same call).  Two calls that can run
  * at the same time on one device, e.g. on different streams, race on it and
- * must be ordered by the caller.  No counterpart in the reference.
+ * must be ordered by the caller.  The looked-up address is kept for the life
+ * of the process, so do not use the library across a cudaDeviceReset of a
+ * device it has run on.  No counterpart in the reference.
  */
 int b2a_decode_paged_noalloc(const void* q, const void* k_pool,
                              const void* v_pool, const int32_t* block_table,
@@ -202,9 +204,25 @@ int b2a_decode_paged_noalloc(const void* q, const void* k_pool,
  * the backward kernel found too little shared memory to align its tiles and
  * did nothing).  Reads and clears the
  * word of the current device; this call synchronises the device.  *flags
- * receives the word.
+ * receives the word.  Returns B2A_ERR_TIMEOUT when bit 0 is set (the outputs
+ * of the calls since the previous check are then undefined), B2A_OK
+ * otherwise (the other bits report bad inputs and leave the status OK).
+ * The reference has no device-side status: it checks only the launch
+ * (cuda/flash_attn_fa3_db_full.cu:399).
  */
 int b2a_device_error(uint32_t* flags);
+
+/*
+ * Self-test of the bounded waits: launches one thread that waits, with a
+ * limit of limit_us microseconds (1 .. 1,000,000), on an mbarrier nothing
+ * arrives at, synchronises `stream` and returns what that wait reported --
+ * B2A_ERR_TIMEOUT when it gave up as intended.  Nothing else is in flight in
+ * that kernel, so the device stays usable afterwards.  It shows that a
+ * pipeline wait that is never satisfied ends as a status on the host instead
+ * of a hang.  No counterpart in the reference (its only checks are host-side,
+ * cuda/flash_attn_fa3_db_full.cu:352-363 and :399).
+ */
+int b2a_selftest_wait_timeout(int limit_us, void* stream);
 
 #ifdef __cplusplus
 }

@@ -79,3 +79,31 @@ def test_python_api_rejects_like_the_reference():
         b200attn.forward_only(q, q, q)
     with pytest.raises(RuntimeError, match="CUDA tensors"):
         b200attn.decode(q[:, :, 0], q, q)
+
+
+def test_selftest_rejects_bad_limit():
+    from b200attn import _lib
+    lib = _lib.load()
+    assert lib.b2a_selftest_wait_timeout(0, None) == 1
+    assert lib.b2a_selftest_wait_timeout(2_000_000, None) == 1
+
+
+def test_device_error_reports_timeout_status(monkeypatch):
+    """(No GPU needed: the library call is faked.)  b2a_device_error returns B2A_ERR_TIMEOUT when bit 0 is set; the Python
+    reader returns the flags and check_device() raises."""
+    import b200attn
+    from b200attn import _lib, attention as A
+    lib = _lib.load()
+
+    class FakeLib:
+        def b2a_device_error(self, p):
+            p._obj.value = 1
+            return _lib.B2A_ERR_TIMEOUT
+
+        def __getattr__(self, n):
+            return getattr(lib, n)
+
+    monkeypatch.setattr(_lib, "load", lambda: FakeLib())
+    assert A.device_error_flags() == 1
+    with pytest.raises(RuntimeError, match="wait timed out"):
+        A.check_device()

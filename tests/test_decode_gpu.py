@@ -154,3 +154,75 @@ def test_config4_full_size_sampled(b2a):
     for b in (0, 33, 63):
         Or, Lr = ora.decode(host(q[b:b + 1, :, 0]), host(k[b:b + 1]), host(v[b:b + 1]))
         assert_parity(O[b:b + 1, :, 0], L[b:b + 1, :, 0], Or, Lr, "float16", 1.0, f"b={b}")
+
+
+def _gather_seq(pool, bt_row, n, page):
+    """[1, Hkv, n, D] contiguous copy (on the device) of one sequence's pages."""
+    np_ = -(-n // page)
+    pages = pool.index_select(0, bt_row[:np_].long())            # [np, Hkv, page, D]
+    return pages.permute(1, 0, 2, 3).reshape(1, pool.shape[1], np_ * page, -1)[:, :, :n]
+
+
+def test_config5a_full_shape_sampled(b2a):
+    """Config 5a at its own shape: B=128, H=32, Hkv=8, D=128 fp16, 16-token pages,
+    seeded lengths U[512, 32768] (two of them set to a page boundary and one past
+    it), pool pages in a seeded random permutation; 64 pages per split (the bench's
+    setting).  The oracle checks the longest sequence, the page-boundary ones and
+    two more."""
+    B, H, Hkv, D, page, pps = 128, 32, 8, 128, 16, 64
+    rng = np.random.default_rng(55)
+    lens = rng.integers(512, 32768 + 1, size=B).astype(np.int64)
+    lens[7], lens[8] = 16384, 16385          # a page boundary and one token past it
+    lens[9] = 32768                          # the maximum length: every slot of its last page
+    npages = -(-lens // page)
+    P = int(npages.sum())
+    perm = torch.randperm(P, generator=torch.Generator().manual_seed(77)).to(torch.int32)
+    bt = torch.zeros(B, int(npages.max()), dtype=torch.int32)
+    pos = 0
+    for b in range(B):
+        bt[b, :npages[b]] = perm[pos:pos + npages[b]]
+        pos += npages[b]
+    bt = bt.cuda()
+    kl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    kp = torch.randn(P, Hkv, page, D, device="cuda", generator=g).half()
+    vp = torch.randn(P, Hkv, page, D, device="cuda", generator=g).half()
+    q = torch.randn(B, H, D, device="cuda", generator=g).half()
+    O, L = b2a.decode_paged(q, kp, vp, bt, kl, pages_per_split=pps)
+    torch.cuda.synchronize()
+    assert b2a.device_error_flags() == 0
+    longest = int(np.argmax(lens))
+    for b in sorted({longest, 7, 8, 9, 0, 100}):
+        n = int(lens[b])
+        k = _gather_seq(kp, bt[b], n, page)
+        v = _gather_seq(vp, bt[b], n, page)
+        Or, Lr = ora.decode(host(q[b:b + 1]), host(k), host(v))
+        assert_parity(O[b:b + 1], L[b:b + 1], Or, Lr, "float16", 1.0, f"b={b} len={n}")
+    del kp, vp
+    torch.cuda.empty_cache()
+
+
+def test_config5b_full_shape_and_eight_way_shard(b2a):
+    """Config 5b at its own shape: B=1, H=32, Hkv=8, KV length 131072 bf16, 32
+    splits, through the one-rank path; then the 8-way sequence shard simulated on
+    one GPU -- split-KV partials of 8 contiguous 16384-token slices, concatenated
+    in sequence order, one combine -- against the same oracle."""
+    H, Hkv, L_, D, S = 32, 8, 131072, 128, 32
+    g = torch.Generator(device="cuda").manual_seed(55)
+    q = torch.randn(1, H, D, device="cuda", generator=g).bfloat16()
+    k = torch.randn(1, Hkv, L_, D, device="cuda", generator=g).bfloat16()
+    v = torch.randn(1, Hkv, L_, D, device="cuda", generator=g).bfloat16()
+    O, L = b2a.decode(q, k, v, splits=S)
+    Or, Lr = ora.decode(host(q), host(k), host(v))
+    assert_parity(O, L, Or, Lr, "bfloat16", 1.0, "config 5b, one rank")
+    world = 8
+    sl = L_ // world
+    parts = [b2a.decode_splitkv(q, k[:, :, r * sl:(r + 1) * sl].contiguous(),
+                                v[:, :, r * sl:(r + 1) * sl].contiguous(), splits=S)
+             for r in range(world)]
+    op = torch.cat([p[0] for p in parts], dim=2)      # [1, H, world*S, D], sequence order
+    lp = torch.cat([p[1] for p in parts], dim=2)
+    O8, L8 = b2a.decode_combine(op, lp, dtype=torch.bfloat16)
+    assert_parity(O8, L8, Or, Lr, "bfloat16", 1.0, "config 5b, 8 shards")
+    torch.cuda.synchronize()
+    assert b2a.device_error_flags() == 0

@@ -224,6 +224,10 @@ SPLIT_CAUSAL_64 = [
     (1, 2, 2, 300, 300, torch.bfloat16),    # 4 blocks x 2 ranks, rank 1 of block 0 empty
     (1, 4, 2, 640, 640, torch.float16),     # 12 blocks x 2 ranks; a rank with tile 1 only
     (1, 1, 1, 129, 4096, torch.bfloat16),   # one block x 8 ranks, causal offset 3967
+    # GQA with Nk > N under a non-zero causal offset: 2 blocks x 4 heads, the
+    # 1100 keys in 9 tiles; in block 0, tile 0 (rows 0-127) sees keys up to
+    # 927, tile 1 up to 1055, so some ranks hold tiles for tile 1 only
+    (1, 4, 2, 300, 1100, torch.bfloat16),
 ]
 
 
