@@ -562,14 +562,16 @@ def kernel_step_times(torch, step, stream, first: int, n: int) -> list:
     return [a.elapsed_time(b) for a, b in evs]
 
 
-SECONDARY = ("2", "4")
+SECONDARY = ("2", "4", "5a", "5b")
 
 
 def run_secondary(args, rank, world, dev, clocks, peaks) -> dict:
-    """Value and roofline of the other headline workloads (config 2, the
-    reference's own headline shape, and config 4, split-KV decode), timed in the
-    same process on the same box: warm-up, then K device-timed steps (max over
-    ranks), then the per-step kernel time for the roofline."""
+    """Value and roofline of the other headline workloads -- config 2 (the
+    reference's own headline shape), config 4 (split-KV decode, batch-sharded),
+    config 5a (paged decode, sequences balanced over ranks) and config 5b (the
+    KV-sharded decode with its NCCL all-gather) -- timed in the same process on
+    the same box: warm-up, then K device-timed steps (max over ranks), then the
+    per-step kernel time for the roofline."""
     import torch
     import torch.distributed as dist
     stream = torch.cuda.current_stream(dev)
@@ -578,7 +580,7 @@ def run_secondary(args, rank, world, dev, clocks, peaks) -> dict:
         if key == args.config:
             continue
         w = make_workload(key, args, rank, world, dev)
-        steps = 50 if w.c["kind"] == "prefill" else 20
+        steps = 50 if w.c["kind"] in ("prefill", "kvshard") else 20
         for i in range(max(args.warmup, 3)):
             w.step(i)
         if world > 1:
@@ -602,8 +604,11 @@ def run_secondary(args, rank, world, dev, clocks, peaks) -> dict:
             "value": round(w.work_per_step * steps * world / (ms / 1e3) / scale, 3),
             "unit": w.unit, "steps": steps, "ms_per_step": round(ms / steps, 5),
             "scaling": "weak" if not w.c["shard"] else "strong",
+            "parallelism": ("replicas" if not w.c["shard"] else "sharded") + f" x{world}",
             "l2": f"{w.nsets} rotating input sets" if w.nsets > 1 else "inputs larger than L2",
             "roofline": roofline_of(w, key, kms, clocks, peaks)}
+        if "collective" in w.workload:
+            out[f"config{key}"]["collective"] = w.workload["collective"]
         del w
         torch.cuda.empty_cache()
     return out

@@ -33,6 +33,9 @@ _SIGNATURES = {
     "b2a_decode_splitkv": (_c_int, [_vp] * 5 + [_c_int] * 6 + [_c_int, _c_float, _vp]),
     # o_part l_part o lse | B H splits D dtype | stream
     "b2a_decode_combine": (_c_int, [_vp] * 4 + [_c_int] * 5 + [_vp]),
+    # o_part l_part o lse | B H splits ranks | rank_stride | D dtype | stream
+    "b2a_decode_combine_ranks": (_c_int, [_vp] * 4 + [_c_int] * 4 + [ctypes.c_int64]
+                                 + [_c_int] * 2 + [_vp]),
     # q kp vp bt lens o_part l_part o lse | B H Hkv D page max_pages num_pages pps | dtype scale stream
     "b2a_decode_paged": (_c_int, [_vp] * 9 + [_c_int] * 8 + [_c_int, _c_float, _vp]),
     # q kp vp bt lens o lse | B H Hkv D page max_pages num_pages pps | dtype scale stream

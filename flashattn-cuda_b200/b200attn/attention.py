@@ -229,12 +229,14 @@ def _check_decode_common(q, k, v):
 
 
 def decode_splitkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, splits: int = 16,
-                   scale: Optional[float] = None):
+                   scale: Optional[float] = None, out=None):
     """Split-KV decode partials.
 
     q [B, H, D] (or [B, H, 1, D]); k, v [B, Hkv, Lkv, D] contiguous KV cache.
     Returns (o_part fp32 [B, H, splits, D], l_part fp32 [B, H, splits]): per
     split the softmax-normalised output and the natural-log sum of exp.
+    `out` = (o_part, l_part): contiguous fp32 tensors of those shapes to write
+    into (e.g. views of a collective's buffer) instead of fresh ones.
     """
     q3, _ = _decode_q(q)
     _check_decode_common(q3, k, v)
@@ -250,8 +252,17 @@ def decode_splitkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, splits: in
         qc = _as(q3, dt)
         kc = _as(k, dt)
         vc = _as(v, dt)
-        o_part = torch.empty((B, H, splits, D), dtype=torch.float32, device=q3.device)
-        l_part = torch.empty((B, H, splits), dtype=torch.float32, device=q3.device)
+        if out is None:
+            o_part = torch.empty((B, H, splits, D), dtype=torch.float32, device=q3.device)
+            l_part = torch.empty((B, H, splits), dtype=torch.float32, device=q3.device)
+        else:
+            o_part, l_part = out
+            if (o_part.shape != (B, H, splits, D) or l_part.shape != (B, H, splits)
+                    or o_part.dtype != torch.float32 or l_part.dtype != torch.float32
+                    or not (o_part.is_contiguous() and l_part.is_contiguous())
+                    or o_part.device != q3.device or l_part.device != q3.device):
+                raise RuntimeError("out must be contiguous fp32 (o_part [B,H,splits,D], "
+                                   "l_part [B,H,splits]) on q's device")
         s = float(D) ** -0.5 if scale is None else float(scale)
         _lib.check(lib.b2a_decode_splitkv(
             qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o_part.data_ptr(), l_part.data_ptr(),
@@ -278,6 +289,31 @@ def decode_combine(o_part: torch.Tensor, l_part: torch.Tensor,
         _lib.check(lib.b2a_decode_combine(op.data_ptr(), lp.data_ptr(), O.data_ptr(),
                                           L.data_ptr(), B, H, S, D, _DT[dtype],
                                           _stream(o_part.device)))
+    return [O, L]
+
+
+def decode_combine_ranks(buf: torch.Tensor, B: int, H: int, splits: int, D: int, ranks: int,
+                         rank_stride: int, dtype: torch.dtype = torch.float16) -> list:
+    """Combine of the partials of `ranks` ranks gathered into one flat fp32 buffer:
+    rank r's chunk starts at buf[r * rank_stride] and holds its o [B,H,splits,D]
+    followed by its l [B,H,splits] (b2a_decode_combine_ranks).  Returns
+    [O (dtype) [B,H,D], L fp32 [B,H]]."""
+    if not buf.is_cuda or buf.dtype != torch.float32 or not buf.is_contiguous():
+        raise RuntimeError("buf must be a contiguous fp32 CUDA tensor")
+    if buf.numel() < ranks * rank_stride or rank_stride < B * H * splits * (D + 1):
+        raise RuntimeError("buf too small for ranks x rank_stride, or rank_stride below "
+                           "B*H*splits*(D+1)")
+    if dtype not in _DT:
+        raise RuntimeError("dtype must be torch.float16 or torch.bfloat16")
+    lib = _lib.load()
+    with _on_device(buf.device):
+        O = torch.empty((B, H, D), dtype=dtype, device=buf.device)
+        L = torch.empty((B, H), dtype=torch.float32, device=buf.device)
+        base = buf.data_ptr()
+        _lib.check(lib.b2a_decode_combine_ranks(base, base + 4 * B * H * splits * D,
+                                                O.data_ptr(), L.data_ptr(), B, H, splits,
+                                                ranks, rank_stride, D, _DT[dtype],
+                                                _stream(buf.device)))
     return [O, L]
 
 

@@ -82,8 +82,10 @@ int kv_append_dispatch(const void* k_new, const void* v_new, void* k_pool, void*
                        const int32_t* block_table, int32_t* kv_lens, int B, int Hkv, int T, int D,
                        int page_size, int max_pages, int num_pages, int advance,
                        cudaStream_t stream);
+// ranks > 1: partials of `ranks` ranks, rank r's o / l blocks `rank_stride`
+// floats after rank r-1's (KV-sharded decode's gathered buffer).
 int combine_dispatch(const float* o_part, const float* l_part, void* o, float* lse, int B, int H,
-                     int splits, int D, int dtype, const int32_t* kv_lens, int tokens_per_split,
-                     cudaStream_t stream);
+                     int splits, int D, int dtype, const int32_t* kv_lens, int tps,
+                     cudaStream_t stream, int ranks = 1, long long rank_stride = 0);
 
 }  // namespace b2a

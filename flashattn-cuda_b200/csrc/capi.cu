@@ -311,6 +311,28 @@ int b2a_decode_combine(const float* o_part, const float* l_part, void* o, float*
                           static_cast<cudaStream_t>(stream));
 }
 
+int b2a_decode_combine_ranks(const float* o_part, const float* l_part, void* o, float* lse, int B,
+                             int H, int splits, int ranks, int64_t rank_stride, int D, int dtype,
+                             void* stream) {
+  t_last_error[0] = 0;
+  B2A_TRY(common_checks(dtype));
+  if (D != 64 && D != 128) return set_error(B2A_ERR_UNSUPPORTED, "Head dimension must be 64 or 128");
+  if (B <= 0 || H <= 0 || splits <= 0 || ranks <= 0)
+    return set_error(B2A_ERR_INVALID_ARG, "B, H, splits and ranks must be > 0");
+  const int64_t block = (int64_t)B * H * splits * D;
+  if (ranks > 1 && rank_stride < block + (int64_t)B * H * splits)
+    return set_error(B2A_ERR_INVALID_ARG,
+                     "rank_stride must cover one rank's o and l partials (B*H*splits*(D+1) floats)");
+  B2A_TRY(check_device_ptr(o_part, "o_part"));
+  B2A_TRY(check_device_ptr(l_part, "l_part", false));
+  if (reinterpret_cast<uintptr_t>(l_part) & 3u)
+    return set_error(B2A_ERR_MISALIGNED, "l_part must be 4-byte aligned");
+  B2A_TRY(check_device_ptr(o, "O"));
+  if (lse != nullptr) B2A_TRY(check_device_ptr(lse, "L"));
+  return combine_dispatch(o_part, l_part, o, lse, B, H, splits, D, dtype, nullptr, 0,
+                          static_cast<cudaStream_t>(stream), ranks, (long long)rank_stride);
+}
+
 int b2a_decode_paged(const void* q, const void* k_pool, const void* v_pool,
                      const int32_t* block_table, const int32_t* kv_lens, float* o_part,
                      float* l_part, void* o, float* lse, int B, int H, int Hkv, int D,

@@ -356,24 +356,34 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-// One CTA per (batch row, query head), one thread per output column.
+// One CTA per (batch row, query head), one thread per output column.  The
+// partials may come from several ranks (KV-sharded decode): rank r's block of
+// [B,H,S,D] o / [B,H,S] l starts r * rank_stride floats after rank 0's, and
+// rank r's splits follow rank r-1's in sequence order (one rank: R = 1).
 template <bool BF16>
 __global__ void combine_kernel(const float* __restrict__ o_part, const float* __restrict__ l_part,
                                void* __restrict__ out, float* __restrict__ lse, int H, int S,
-                               int D, const int32_t* __restrict__ kv_lens, int tps) {
+                               int D, const int32_t* __restrict__ kv_lens, int tps, int R,
+                               long long rank_stride) {
   using T = typename Elem<BF16>::T;
   const int bh = blockIdx.x;
-  int ns = S;
+  int ns = S;  // splits per rank
   if (kv_lens != nullptr) ns = max(0, min(S, (kv_lens[bh / H] + tps - 1) / tps));
-  const float* lp = l_part + (size_t)bh * S;
   float M = -INFINITY;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, lp[s]);
+  for (int r = 0; r < R; ++r) {
+    const float* lp = l_part + r * rank_stride + (size_t)bh * S;
+    for (int s = 0; s < ns; ++s) M = fmaxf(M, lp[s]);
+  }
   const int d = threadIdx.x;
   float sum = 0.f, acc = 0.f;
-  for (int s = 0; s < ns; ++s) {
-    const float w = (lp[s] == -INFINITY) ? 0.f : expf(lp[s] - M);
-    sum += w;
-    if (d < D) acc += w * o_part[((size_t)bh * S + s) * D + d];
+  for (int r = 0; r < R; ++r) {
+    const float* lp = l_part + r * rank_stride + (size_t)bh * S;
+    const float* op = o_part + r * rank_stride + (size_t)bh * S * D;
+    for (int s = 0; s < ns; ++s) {
+      const float w = (lp[s] == -INFINITY) ? 0.f : expf(lp[s] - M);
+      sum += w;
+      if (d < D) acc += w * op[(size_t)s * D + d];
+    }
   }
   // no key at all (an empty sequence): O = 0, L = -inf
   if (d < D)
@@ -456,14 +466,14 @@ int decode_dispatch(const void* q, const void* k, const void* v, const int32_t* 
 
 int combine_dispatch(const float* o_part, const float* l_part, void* o, float* lse, int B, int H,
                      int splits, int D, int dtype, const int32_t* kv_lens, int tps,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, int ranks, long long rank_stride) {
   const unsigned threads = (unsigned)((D + 31) / 32 * 32);
   if (dtype == B2A_BF16)
     decode::combine_kernel<true><<<B * H, threads, 0, stream>>>(o_part, l_part, o, lse, H, splits,
-                                                                D, kv_lens, tps);
+                                                                D, kv_lens, tps, ranks, rank_stride);
   else
     decode::combine_kernel<false><<<B * H, threads, 0, stream>>>(o_part, l_part, o, lse, H, splits,
-                                                                 D, kv_lens, tps);
+                                                                 D, kv_lens, tps, ranks, rank_stride);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "combine kernel launch");
   return B2A_OK;

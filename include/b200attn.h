@@ -136,6 +136,19 @@ int b2a_decode_combine(const float* o_part, const float* l_part, void* o,
                        void* stream);
 
 /*
+ * LSE-weighted combine of partials gathered from `ranks` ranks (KV-sharded
+ * decode): rank r's o block [B,H,splits,D] starts r*rank_stride floats after
+ * o_part and its l block [B,H,splits] r*rank_stride floats after l_part, and
+ * rank r's splits follow rank r-1's in sequence order.  This reads the buffer
+ * an all-gather of per-rank [o | l] chunks of rank_stride floats produces,
+ * without a reordering copy.  ranks == 1 is b2a_decode_combine.  Same identity
+ * as b2a_decode_combine (cuda/flash_attn_fa3_db_full.cu:261-284, :340).
+ */
+int b2a_decode_combine_ranks(const float* o_part, const float* l_part, void* o,
+                             float* lse, int B, int H, int splits, int ranks,
+                             int64_t rank_stride, int D, int dtype, void* stream);
+
+/*
  * Paged decode: as split-KV decode, but token t of sequence b lives in page
  * block_table[b, t / page_size] at slot t % page_size of k_pool/v_pool
  * ([P,Hkv,page_size,D]).  Sequence b has kv_lens[b] >= 1 tokens.  Each split

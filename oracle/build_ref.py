@@ -9,7 +9,7 @@ instead of sm_89 (an sm_89 cubin does not load on a B200).  Only the source
 file is read from the reference checkout; its setup.py is not run.  Output:
 oracle/_ref/flash_attn_fa3_db_full.so (git-ignored; it travels to the GPU box).
 
-    python oracle/build_ref.py [/path/to/reference]
+    python oracle/build_ref.py /path/to/reference   (or B2A_REFERENCE_ROOT=...)
 """
 from __future__ import annotations
 
@@ -27,7 +27,7 @@ def so_path() -> str:
     return os.path.join(OUT, NAME + ".so")
 
 
-def build(ref_root: str = "/root/reference") -> str:
+def build(ref_root: str) -> str:
     src = os.path.join(ref_root, "cuda", "flash_attn_fa3_db_full.cu")
     if not os.path.exists(src):
         raise FileNotFoundError(src)
@@ -59,4 +59,7 @@ def load_built():
 
 
 if __name__ == "__main__":
-    print(build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("B2A_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: build_ref.py <reference checkout> (or set B2A_REFERENCE_ROOT)")
+    print(build(root))

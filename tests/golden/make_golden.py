@@ -117,4 +117,7 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("B2A_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py <reference checkout> (or set B2A_REFERENCE_ROOT)")
+    main(root)

@@ -244,3 +244,41 @@ def test_split_kv_d64_causal(b2a, B, H, Hkv, N, Nk, dt):
     assert torch.equal(b2a.forward_only(q, k, v, causal=True), O)
     torch.cuda.synchronize()
     assert b2a.device_error_flags() == 0
+
+
+# Dense D = 128 launches are persistent: each CTA walks a static list of
+# (head, 256-row block) blocks -- pairs (nqb-1-j, j) per head when there are
+# many, a heaviest-first boustrophedon deal of single blocks when there are few,
+# one block per item without a mask.  The varlen form of the same kernel runs
+# one block per CTA, and with equal lengths its output is bitwise equal to the
+# dense one: so every block of every head must be computed exactly once.
+SCHEDULE_CASES = [
+    # B, H, Hkv, N, causal   (schedule on a 148-SM B200)
+    (1, 64, 8, 7936, True),    # pairs: 64 heads x 16 items, the odd block 15 alone
+    (2, 4, 2, 3000, True),     # few items: single blocks dealt heaviest first
+    (3, 5, 5, 1100, False),    # no mask: one block per item, head-major
+]
+
+
+@pytest.mark.parametrize("B,H,Hkv,N,causal", SCHEDULE_CASES, ids=lambda x: str(x))
+def test_persistent_schedule_covers_every_block_once(b2a, B, H, Hkv, N, causal):
+    D = 128
+    g = torch.Generator(device="cuda").manual_seed(N)
+    q = torch.randn(B, H, N, D, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, N, D, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, N, D, device="cuda", generator=g).to(torch.bfloat16)
+    b2a.device_error_flags()
+    O, L = b2a.forward(q, k, v, causal=causal)
+    # the same batch through the one-block-per-CTA varlen launch
+    pack = lambda t: t.permute(0, 2, 1, 3).reshape(B * N, t.shape[1], D).contiguous()
+    cu = torch.arange(0, (B + 1) * N, N, dtype=torch.int32, device="cuda")
+    Ov, Lv = b2a.forward_varlen(pack(q), pack(k), pack(v), cu, cu, N, causal=causal)
+    assert torch.equal(pack(O), Ov)
+    assert torch.equal(L.permute(1, 0, 2).reshape(H, B * N), Lv)
+    rows = [0, 255, 256, N // 2, N - 1]
+    for b, h in [(0, 0), (B - 1, H - 1)]:
+        Or, Lr = ora.attention_rows(host(q), host(k), host(v), b, h, rows, scale=D ** -0.5,
+                                    causal=causal)
+        assert_parity(O[b, h, rows], L[b, h, rows], Or, Lr, "bfloat16", 1.0, f"b{b}h{h}")
+    torch.cuda.synchronize()
+    assert b2a.device_error_flags() == 0

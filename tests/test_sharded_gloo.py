@@ -32,12 +32,15 @@ def _free_port() -> int:
     return p
 
 
-def _oracle_partials(q, k, v, splits, scale):
+def _oracle_partials(q, k, v, splits, scale, out):
     op, lp = ora.decode_splitkv_partials(q.numpy(), k.numpy(), v.numpy(), splits, scale)
-    return torch.from_numpy(op).float(), torch.from_numpy(lp).float()
+    out[0].copy_(torch.from_numpy(op))
+    out[1].copy_(torch.from_numpy(lp))
 
 
-def _oracle_combine(o, l, dt):
+def _oracle_combine(buf, world, B_, H_, S, D_, dt):
+    from b200attn.sharded import unpack_gathered
+    o, l = unpack_gathered(buf, world, B_, H_, S, D_)
     O, Lse = ora.combine(o.numpy(), l.numpy())
     return torch.from_numpy(O).float(), torch.from_numpy(Lse).float()
 

@@ -42,6 +42,33 @@ def test_sharded_world1_equals_decode():
     assert_parity(O, Lse, Or, Lr, "bfloat16")
 
 
+@pytest.mark.parametrize("world", [3, 8])
+def test_gathered_chunks_combine_in_place(world):
+    """The KV-sharded step's data path on one GPU: each emulated rank's split-KV
+    kernel writes its partials into its chunk of one flat buffer (the layout the
+    in-place all-gather leaves on every rank), and combine_kernel reads the
+    chunks where they lie -- no packing or reordering copy -- matching the
+    oracle on the whole sequence."""
+    import b200attn
+    from b200attn.attention import decode_combine_ranks
+    from b200attn.sharded import chunk_views, partials_chunk
+    q, k, v = (torch.from_numpy(a).to(torch.bfloat16).cuda() for a in _inputs())
+    S = 4
+    c = partials_chunk(B, H, S, D)
+    buf = torch.full((world * c,), float("nan"), dtype=torch.float32, device="cuda")
+    bnd = np.linspace(0, L, world + 1).astype(int)
+    for r in range(world):
+        ks = k[:, :, bnd[r]:bnd[r + 1]].contiguous()
+        vs = v[:, :, bnd[r]:bnd[r + 1]].contiguous()
+        b200attn.decode_splitkv(q, ks, vs, splits=S, out=chunk_views(buf[r * c:(r + 1) * c],
+                                                                     B, H, S, D))
+    O, Lse = decode_combine_ranks(buf, B, H, S, D, world, c, torch.bfloat16)
+    Or, Lr = ora.decode(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy())
+    assert_parity(O, Lse, Or, Lr, "bfloat16", 1.0, f"{world} emulated ranks")
+    torch.cuda.synchronize()
+    assert b200attn.device_error_flags() == 0
+
+
 def _worker(rank, world, port, out_dir):
     try:
         root = os.path.join(os.path.dirname(os.path.abspath(__file__)), "..")
