@@ -8,7 +8,7 @@ collective.  The same line carries a `secondary` object with config 2 (the
 reference's headline shape, B=1 H=8 N=4096 D=64 fp16 non-causal, which
 bench/bench_fa3_headline.py of the reference times as forward()+L) and config 4
 (split-KV GQA decode), timed in the same process.  A step is one forward over
-one batch.  Other main configs: --config 1|2|3s|4|4s|5a|5b|6|6s|7|7s|7m.
+one batch.  Other main configs: --config 1|2|3m|3s|4|4s|5a|5b|6|6s|7|7s|7m.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
 
@@ -54,7 +54,12 @@ CONFIGS = {
               shard=False, name="config2: prefill fwd B=1 H=8 N=4096 D=64 fp16 non-causal"),
     "3": dict(kind="prefill", B=4, H=32, Hkv=32, N=8192, D=128, dtype="bfloat16", causal=True,
               shard=True, name="config3: prefill fwd B=4 H=32 N=8192 D=128 bf16 causal"),
-    # config 3 at 1/4 of the heads (201 MB of Q/K/V, still > L2): the case ncu section captures run on
+    # config 3 at half the batch (403 MB of Q/K/V): 1024 pair items on 148 SMs, the schedule
+    # config 3 itself runs (pairs); the case ncu section captures of that schedule run on
+    "3m": dict(kind="prefill", B=2, H=32, Hkv=32, N=8192, D=128, dtype="bfloat16", causal=True,
+               shard=True, name="config3-half: prefill fwd B=2 H=32 N=8192 D=128 bf16 causal"),
+    # config 3 at 1/4 of the batch (201 MB of Q/K/V, still > L2): 32 heads per GPU, the
+    # share of config 3 at 4 GPUs (heaviest-first single-block schedule)
     "3s": dict(kind="prefill", B=1, H=32, Hkv=32, N=8192, D=128, dtype="bfloat16", causal=True,
                shard=True, name="config3-small: prefill fwd B=1 H=32 N=8192 D=128 bf16 causal"),
     "4": dict(kind="decode", B=64, H=32, Hkv=8, L=16384, D=128, dtype="float16", splits=16,
