@@ -462,7 +462,7 @@ def make_workload(cfg_key, args, rank, world, dev):
 
         workload = dict(workload=c["name"], B=B, H=H, Hkv=Hkv, L=c["L"], L_per_rank=Ll, D=D,
                         splits_per_rank=c["splits"], dtype=c["dtype"],
-                        collective="all_gather_into_tensor of [B,H,S,D+1] fp32 partials"
+                        collective="merged partials exchanged by one kernel over NVLink peer memory (B*H*(D+1) floats per rank)"
                                    if world > 1 else "none (1 rank)",
                         cuda_graph=bool(args.graph))
     else:  # paged

@@ -33,6 +33,16 @@ _SIGNATURES = {
     "b2a_decode_splitkv": (_c_int, [_vp] * 5 + [_c_int] * 6 + [_c_int, _c_float, _vp]),
     # o_part l_part o lse | B H splits D dtype | stream
     "b2a_decode_combine": (_c_int, [_vp] * 4 + [_c_int] * 5 + [_vp]),
+    "b2a_exchange_bytes": (ctypes.c_int64, [_c_int] * 4),
+    "b2a_exchange_alloc": (_c_int, [ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p), _vp]),
+    "b2a_exchange_open": (_c_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "b2a_exchange_close": (_c_int, [_vp]),
+    "b2a_exchange_free": (_c_int, [_vp]),
+    # o_part l_part peers | rank world | o lse | B H splits D dtype | stream
+    "b2a_decode_exchange_combine": (_c_int, [_vp] * 3 + [_c_int] * 2 + [_vp] * 2 + [_c_int] * 5
+                                    + [_vp]),
+    # o_part l_part o_merged l_merged | B H splits D | stream
+    "b2a_decode_merge_splits": (_c_int, [_vp] * 4 + [_c_int] * 4 + [_vp]),
     # o_part l_part o lse | B H splits ranks | rank_stride | D dtype | stream
     "b2a_decode_combine_ranks": (_c_int, [_vp] * 4 + [_c_int] * 4 + [ctypes.c_int64]
                                  + [_c_int] * 2 + [_vp]),

@@ -292,6 +292,33 @@ def decode_combine(o_part: torch.Tensor, l_part: torch.Tensor,
     return [O, L]
 
 
+def decode_merge_splits(o_part: torch.Tensor, l_part: torch.Tensor, out=None):
+    """Merge split partials o [B,H,S,D], l [B,H,S] (fp32) into one partial of the
+    same form: (o [B,H,D] fp32, normalised, l [B,H] = log sum exp), written into
+    `out` = (o, l) when given (b2a_decode_merge_splits)."""
+    if not (o_part.is_cuda and l_part.is_cuda):
+        raise RuntimeError("o_part/l_part must be CUDA tensors")
+    if o_part.dim() != 4 or l_part.shape != o_part.shape[:3]:
+        raise RuntimeError("o_part must be [B, H, S, D] and l_part [B, H, S]")
+    B, H, S, D = o_part.shape
+    lib = _lib.load()
+    with _on_device(o_part.device):
+        op = o_part.float().contiguous()
+        lp = l_part.float().contiguous()
+        if out is None:
+            om = torch.empty((B, H, D), dtype=torch.float32, device=o_part.device)
+            lm = torch.empty((B, H), dtype=torch.float32, device=o_part.device)
+        else:
+            om, lm = out
+            if (om.numel() != B * H * D or lm.numel() != B * H or om.dtype != torch.float32
+                    or lm.dtype != torch.float32 or not (om.is_contiguous() and lm.is_contiguous())):
+                raise RuntimeError("out must be contiguous fp32 tensors of B*H*D and B*H elements")
+        _lib.check(lib.b2a_decode_merge_splits(op.data_ptr(), lp.data_ptr(), om.data_ptr(),
+                                               lm.data_ptr(), B, H, S, D,
+                                               _stream(o_part.device)))
+    return om, lm
+
+
 def decode_combine_ranks(buf: torch.Tensor, B: int, H: int, splits: int, D: int, ranks: int,
                          rank_stride: int, dtype: torch.dtype = torch.float16) -> list:
     """Combine of the partials of `ranks` ranks gathered into one flat fp32 buffer:

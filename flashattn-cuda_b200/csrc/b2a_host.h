@@ -44,6 +44,7 @@ int take_error_flags_kvcache(uint32_t* flags);
 int take_error_flags_backward(uint32_t* flags);
 int take_error_flags_decode(uint32_t* flags);
 int take_error_flags_selftest(uint32_t* flags);
+int take_error_flags_exchange(uint32_t* flags);
 
 // Defines take_error_flags_<unit>() for the unit that expands it.
 #define B2A_DEFINE_ERROR_READER(unit)                                          \
@@ -82,6 +83,8 @@ int kv_append_dispatch(const void* k_new, const void* v_new, void* k_pool, void*
                        const int32_t* block_table, int32_t* kv_lens, int B, int Hkv, int T, int D,
                        int page_size, int max_pages, int num_pages, int advance,
                        cudaStream_t stream);
+// combine_dispatch's dtype for an fp32 merged partial (o, lse) instead of O.
+constexpr int kCombineF32 = 100;
 // ranks > 1: partials of `ranks` ranks, rank r's o / l blocks `rank_stride`
 // floats after rank r-1's (KV-sharded decode's gathered buffer).
 int combine_dispatch(const float* o_part, const float* l_part, void* o, float* lse, int B, int H,

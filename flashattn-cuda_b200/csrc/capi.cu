@@ -333,6 +333,23 @@ int b2a_decode_combine_ranks(const float* o_part, const float* l_part, void* o, 
                           static_cast<cudaStream_t>(stream), ranks, (long long)rank_stride);
 }
 
+int b2a_decode_merge_splits(const float* o_part, const float* l_part, float* o_merged,
+                            float* l_merged, int B, int H, int splits, int D, void* stream) {
+  t_last_error[0] = 0;
+  B2A_TRY(common_checks(B2A_F16));
+  if (D != 64 && D != 128) return set_error(B2A_ERR_UNSUPPORTED, "Head dimension must be 64 or 128");
+  if (B <= 0 || H <= 0 || splits <= 0)
+    return set_error(B2A_ERR_INVALID_ARG, "B, H and splits must be > 0");
+  B2A_TRY(check_device_ptr(o_part, "o_part"));
+  B2A_TRY(check_device_ptr(l_part, "l_part"));
+  B2A_TRY(check_device_ptr(o_merged, "o_merged"));
+  B2A_TRY(check_device_ptr(l_merged, "l_merged", false));
+  if (reinterpret_cast<uintptr_t>(l_merged) & 3u)
+    return set_error(B2A_ERR_MISALIGNED, "l_merged must be 4-byte aligned");
+  return combine_dispatch(o_part, l_part, o_merged, l_merged, B, H, splits, D, kCombineF32,
+                          nullptr, 0, static_cast<cudaStream_t>(stream));
+}
+
 int b2a_decode_paged(const void* q, const void* k_pool, const void* v_pool,
                      const int32_t* block_table, const int32_t* kv_lens, float* o_part,
                      float* l_part, void* o, float* lse, int B, int H, int Hkv, int D,
@@ -441,6 +458,7 @@ int b2a_device_error(uint32_t* flags) {
   B2A_TRY(take_error_flags_backward(&v));
   B2A_TRY(take_error_flags_decode(&v));
   B2A_TRY(take_error_flags_selftest(&v));
+  B2A_TRY(take_error_flags_exchange(&v));
   *flags = v;
   if (v & 1u) {
     char buf[160];

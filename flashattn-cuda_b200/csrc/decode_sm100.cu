@@ -356,38 +356,90 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-// One CTA per (batch row, query head), one thread per output column.  The
-// partials may come from several ranks (KV-sharded decode): rank r's block of
-// [B,H,S,D] o / [B,H,S] l starts r * rank_stride floats after rank 0's, and
-// rank r's splits follow rank r-1's in sequence order (one rank: R = 1).
-template <bool BF16>
-__global__ void combine_kernel(const float* __restrict__ o_part, const float* __restrict__ l_part,
-                               void* __restrict__ out, float* __restrict__ lse, int H, int S,
-                               int D, const int32_t* __restrict__ kv_lens, int tps, int R,
-                               long long rank_stride) {
-  using T = typename Elem<BF16>::T;
+// One CTA per (batch row, query head).  The partials may come from several
+// ranks (KV-sharded decode): rank r's block of [B,H,S,D] o / [B,H,S] l starts
+// r * rank_stride floats after rank 0's, and rank r's splits follow rank r-1's
+// in sequence order (one rank: R = 1).
+// OUT: 0 fp16 O, 1 bf16 O, 2 fp32 O (a merged partial: o normalised by its
+// own sum, lse = log sum exp over all splits -- the form of one split).
+// kCombineThreads threads: the (rank, split) entries are spread over the
+// threads for the max and the weights (one load each, all in flight at once),
+// and every output column then sums its entries with several loads in flight,
+// so the latency of one partial's load is paid a few times, not once per split.
+constexpr int kCombineThreads = 128;
+constexpr int kCombineChunk = 1024;  // weights held in shared memory at a time
+
+__device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, w) : v + w;
+  }
+  const int warp = threadIdx.x >> 5;
+  __syncthreads();  // red may still be read by a previous reduction
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  v = red[0];
+#pragma unroll
+  for (int i = 1; i < kCombineThreads / 32; ++i) v = is_max ? fmaxf(v, red[i]) : v + red[i];
+  return v;
+}
+
+template <int OUT>
+__global__ void __launch_bounds__(kCombineThreads)
+    combine_kernel(const float* __restrict__ o_part, const float* __restrict__ l_part,
+                   void* __restrict__ out, float* __restrict__ lse, int H, int S, int D,
+                   const int32_t* __restrict__ kv_lens, int tps, int R, long long rank_stride) {
+  __shared__ float sw[kCombineChunk];
+  __shared__ float red[kCombineThreads / 32];
   const int bh = blockIdx.x;
   int ns = S;  // splits per rank
   if (kv_lens != nullptr) ns = max(0, min(S, (kv_lens[bh / H] + tps - 1) / tps));
-  float M = -INFINITY;
-  for (int r = 0; r < R; ++r) {
-    const float* lp = l_part + r * rank_stride + (size_t)bh * S;
-    for (int s = 0; s < ns; ++s) M = fmaxf(M, lp[s]);
-  }
+  const int n = R * ns;  // entries (rank r, split s) = r * ns + s
+  auto lp = [&](int i) {
+    return l_part + (i / ns) * rank_stride + (size_t)bh * S + (i % ns);
+  };
+  auto op = [&](int i) {
+    return o_part + (i / ns) * rank_stride + ((size_t)bh * S + (i % ns)) * D;
+  };
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += kCombineThreads) m = fmaxf(m, *lp(i));
+  const float M = block_reduce(m, red, true);
   const int d = threadIdx.x;
-  float sum = 0.f, acc = 0.f;
-  for (int r = 0; r < R; ++r) {
-    const float* lp = l_part + r * rank_stride + (size_t)bh * S;
-    const float* op = o_part + r * rank_stride + (size_t)bh * S * D;
-    for (int s = 0; s < ns; ++s) {
-      const float w = (lp[s] == -INFINITY) ? 0.f : expf(lp[s] - M);
-      sum += w;
-      if (d < D) acc += w * op[(size_t)s * D + d];
+  float psum = 0.f, acc = 0.f;
+  for (int c0 = 0; c0 < n; c0 += kCombineChunk) {
+    const int cn = min(kCombineChunk, n - c0);
+    __syncthreads();  // the previous chunk's weights are consumed
+    for (int i = threadIdx.x; i < cn; i += kCombineThreads) {
+      const float l = *lp(c0 + i);
+      const float w = (l == -INFINITY) ? 0.f : expf(l - M);
+      sw[i] = w;
+      psum += w;
+    }
+    __syncthreads();
+    if (d < D) {
+      int i = 0;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      for (; i + 4 <= cn; i += 4) {
+        a0 += sw[i] * op(c0 + i)[d];
+        a1 += sw[i + 1] * op(c0 + i + 1)[d];
+        a2 += sw[i + 2] * op(c0 + i + 2)[d];
+        a3 += sw[i + 3] * op(c0 + i + 3)[d];
+      }
+      for (; i < cn; ++i) a0 += sw[i] * op(c0 + i)[d];
+      acc += (a0 + a1) + (a2 + a3);
     }
   }
+  const float sum = block_reduce(psum, red, false);
   // no key at all (an empty sequence): O = 0, L = -inf
-  if (d < D)
-    reinterpret_cast<T*>(out)[(size_t)bh * D + d] = Elem<BF16>::from(sum > 0.f ? acc / sum : 0.f);
+  if (d < D) {
+    const float o = sum > 0.f ? acc / sum : 0.f;
+    if constexpr (OUT == 2)
+      reinterpret_cast<float*>(out)[(size_t)bh * D + d] = o;
+    else
+      reinterpret_cast<typename Elem<OUT == 1>::T*>(out)[(size_t)bh * D + d] =
+          Elem<OUT == 1>::from(o);
+  }
   if (lse != nullptr && d == 0) lse[bh] = sum > 0.f ? M + logf(sum) : -INFINITY;
 }
 
@@ -467,13 +519,14 @@ int decode_dispatch(const void* q, const void* k, const void* v, const int32_t* 
 int combine_dispatch(const float* o_part, const float* l_part, void* o, float* lse, int B, int H,
                      int splits, int D, int dtype, const int32_t* kv_lens, int tps,
                      cudaStream_t stream, int ranks, long long rank_stride) {
-  const unsigned threads = (unsigned)((D + 31) / 32 * 32);
-  if (dtype == B2A_BF16)
-    decode::combine_kernel<true><<<B * H, threads, 0, stream>>>(o_part, l_part, o, lse, H, splits,
-                                                                D, kv_lens, tps, ranks, rank_stride);
-  else
-    decode::combine_kernel<false><<<B * H, threads, 0, stream>>>(o_part, l_part, o, lse, H, splits,
-                                                                 D, kv_lens, tps, ranks, rank_stride);
+  const unsigned threads = decode::kCombineThreads;  // >= D
+  auto go = [&](auto kern) {
+    kern<<<B * H, threads, 0, stream>>>(o_part, l_part, o, lse, H, splits, D, kv_lens, tps, ranks,
+                                        rank_stride);
+  };
+  if (dtype == kCombineF32) go(decode::combine_kernel<2>);
+  else if (dtype == B2A_BF16) go(decode::combine_kernel<1>);
+  else go(decode::combine_kernel<0>);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "combine kernel launch");
   return B2A_OK;

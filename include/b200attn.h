@@ -136,6 +136,19 @@ int b2a_decode_combine(const float* o_part, const float* l_part, void* o,
                        void* stream);
 
 /*
+ * Merge of `splits` split partials into ONE partial of the same form, in fp32:
+ * o_merged [B,H,D] = sum_s exp(l_s - L) o_s and l_merged [B,H] = L =
+ * log sum_s exp(l_s).  A KV-sharded rank merges its own splits with this
+ * before the exchange, so that it sends B*H*(D+1) floats instead of
+ * B*H*splits*(D+1); b2a_decode_combine_ranks with splits = 1 then combines
+ * the ranks.  Same identity as b2a_decode_combine
+ * (cuda/flash_attn_fa3_db_full.cu:261-284, :340), fp32 output.
+ */
+int b2a_decode_merge_splits(const float* o_part, const float* l_part,
+                            float* o_merged, float* l_merged, int B, int H,
+                            int splits, int D, void* stream);
+
+/*
  * LSE-weighted combine of partials gathered from `ranks` ranks (KV-sharded
  * decode): rank r's o block [B,H,splits,D] starts r*rank_stride floats after
  * o_part and its l block [B,H,splits] r*rank_stride floats after l_part, and
@@ -147,6 +160,37 @@ int b2a_decode_combine(const float* o_part, const float* l_part, void* o,
 int b2a_decode_combine_ranks(const float* o_part, const float* l_part, void* o,
                              float* lse, int B, int H, int splits, int ranks,
                              int64_t rank_stride, int D, int dtype, void* stream);
+
+/*
+ * KV-sharded decode's exchange step as ONE kernel over NVLink peer memory.
+ * Each of `world` ranks (one GPU each, one process each) owns an exchange
+ * buffer of b2a_exchange_bytes(B, H, D, world) bytes made by
+ * b2a_exchange_alloc, which also fills a 64-byte CUDA IPC handle; the ranks
+ * swap handles (any host channel) and map each other's buffers with
+ * b2a_exchange_open.  `peers` is a device array of `world` uint64 addresses,
+ * peers[r] = rank r's buffer as mapped here (peers[rank] = the own buffer).
+ * A call merges this rank's split partials o_part [B,H,splits,D] / l_part
+ * [B,H,splits] (from b2a_decode_splitkv on its contiguous KV slice), stores
+ * the merged partial into every rank's buffer, waits (bounded, 1 s; bit 0 of
+ * the device error word on timeout) for every rank's, and writes O [B,H,D]
+ * (dtype) and lse [B,H] (may be NULL) -- identical on every rank.  Every rank
+ * must make the same sequence of calls with the same B, H, D; calls on one
+ * rank must be ordered (one stream); nothing is reset between calls.  It
+ * replaces the all-gather of partials plus combine: the combine identity is
+ * the online-softmax rescale of cuda/flash_attn_fa3_db_full.cu:261-284 and
+ * :340; the reference has no multi-GPU code.  b2a_exchange_close unmaps a
+ * peer buffer and b2a_exchange_free frees the own one (after every peer has
+ * stopped using it).
+ */
+int64_t b2a_exchange_bytes(int B, int H, int D, int world);
+int b2a_exchange_alloc(int64_t bytes, void** ptr, void* ipc_handle);
+int b2a_exchange_open(const void* ipc_handle, void** ptr);
+int b2a_exchange_close(void* peer_ptr);
+int b2a_exchange_free(void* ptr);
+int b2a_decode_exchange_combine(const float* o_part, const float* l_part,
+                                const uint64_t* peers, int rank, int world,
+                                void* o, float* lse, int B, int H, int splits,
+                                int D, int dtype, void* stream);
 
 /*
  * Paged decode: as split-KV decode, but token t of sequence b lives in page
@@ -215,7 +259,8 @@ int b2a_decode_paged_noalloc(const void* q, const void* k_pool,
  * bit 2: a KV append found no page for a position; bit 3: a varlen sequence
  * was longer than max_seqlen_q or cu_seqlens was not non-decreasing; bit 4:
  * the backward kernel found too little shared memory to align its tiles and
- * did nothing).  Reads and clears the
+ * did nothing; bit 0 is also set when b2a_decode_exchange_combine gave up
+ * waiting for a peer).  Reads and clears the
  * word of the current device; this call synchronises the device.  *flags
  * receives the word.  Returns B2A_ERR_TIMEOUT when bit 0 is set (the outputs
  * of the calls since the previous check are then undefined), B2A_OK

@@ -32,15 +32,21 @@ def _free_port() -> int:
     return p
 
 
-def _oracle_partials(q, k, v, splits, scale, out):
+def _oracle_partials(q, k, v, splits, scale):
     op, lp = ora.decode_splitkv_partials(q.numpy(), k.numpy(), v.numpy(), splits, scale)
-    out[0].copy_(torch.from_numpy(op))
-    out[1].copy_(torch.from_numpy(lp))
+    return torch.from_numpy(op).float(), torch.from_numpy(lp).float()
 
 
-def _oracle_combine(buf, world, B_, H_, S, D_, dt):
+def _oracle_merge(o, l, out):
+    # a merged partial is the combine's O (normalised) and L = log sum exp
+    O, Lse = ora.combine(o.numpy(), l.numpy())
+    out[0].copy_(torch.from_numpy(O))
+    out[1].copy_(torch.from_numpy(Lse))
+
+
+def _oracle_combine(buf, world, B_, H_, D_, dt):
     from b200attn.sharded import unpack_gathered
-    o, l = unpack_gathered(buf, world, B_, H_, S, D_)
+    o, l = unpack_gathered(buf, world, B_, H_, D_)
     O, Lse = ora.combine(o.numpy(), l.numpy())
     return torch.from_numpy(O).float(), torch.from_numpy(Lse).float()
 
@@ -66,7 +72,8 @@ def _worker(rank, world, port, mode, out_dir):
         if mode == "dead" and rank == 1:
             os._exit(0)                                        # leaves before the collective
         O, Lse = decode_kv_sharded(torch.from_numpy(q), ks, vs, splits=splits,
-                                   local_partials=_oracle_partials, combine=_oracle_combine)
+                                   local_partials=_oracle_partials, merge=_oracle_merge,
+                                   combine=_oracle_combine)
         Or, Lr = ora.decode(q, k, v)
         np.testing.assert_allclose(O.numpy(), Or, rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(Lse.numpy(), Lr, rtol=1e-6, atol=1e-6)
