@@ -1,8 +1,9 @@
 """KV-sharded decode (config 5b's exchange step) on CPU ranks with the gloo
-backend.  The per-rank partials and the combine come from the oracle here
-(the CUDA kernels need a GPU), so these tests cover the host-side logic: the
-sequence split, the packed all-gather, the reordering of the gathered
-partials, shape agreement across ranks, and what a surviving rank sees when a
+backend, on the collective form of the exchange.  The per-rank partials, the
+merge and the combine come from the oracle here (the CUDA kernels need a GPU),
+so these tests cover the host-side logic: the sequence split, the per-rank
+merge into its chunk, the in-place all-gather of the chunks, their order,
+shape agreement across ranks, and what a surviving rank sees when a
 peer dies before the collective (a bounded error, never a hang)."""
 from __future__ import annotations
 
