@@ -5,23 +5,24 @@
 // Each rank owns one exchange buffer, mapped into every other rank's address
 // space (CUDA IPC over NVLink / NVSwitch).  For B*H rows, world W and head
 // dim D its layout is
-//   data  [2][W][B*H][D+1] fp32  slot (parity, source rank, row): o then l
-//   flags [W][B*H]         u32   call count the source rank has delivered
-//   seen  [B*H]            u32   calls this rank has completed, per row
+//   data  [2][W][B*H][D+1] of {value, call}  8-byte words: slot (parity,
+//         source rank, row) holds o[0..D-1] then l, each tagged with the call
+//         count it belongs to
+//   seen  [B*H] u32   calls this rank has completed, per row
 // One CTA per row (b, h):
 //   1. merge the rank's S split partials (o_s, l_s) into one (o, l) -- the
 //      online-softmax rescale of cuda/flash_attn_fa3_db_full.cu:261-284;
-//   2. target = seen + 1, parity = target & 1; store (o, l) into slot
-//      (parity, this rank, row) of EVERY rank's buffer (peer stores), fence at
-//      system scope, then store `target` into this rank's flag of the row in
-//      every rank's buffer;
-//   3. wait (bounded) until every rank's flag for the row here reaches
-//      `target`, then combine the W slots from local memory into O, L;
-//   4. seen = target.
+//   2. call = seen + 1, parity = call & 1; store {value, call} words into slot
+//      (parity, this rank, row) of EVERY rank's buffer (peer stores);
+//   3. poll (bounded) the W slots of the row in this rank's own buffer until
+//      every word carries `call`, then combine them into O, L;
+//   4. seen = call.
+// An 8-byte aligned store is seen whole, so a word whose tag matches holds
+// the matching value: no fence and no separate flag round trip are needed.
 // Two parities suffice: a rank can be at most one call ahead of a slowest
-// peer (finishing call n needs every peer's call-n signal, which a peer sends
+// peer (finishing call n needs every peer's call-n words, which a peer sends
 // only after it has finished call n-1 and its reads of the other parity).
-// Flags only grow, so nothing is reset between calls.  No TMA or bulk copy
+// Tags only grow, so nothing is reset between calls.  No TMA or bulk copy
 // touches peer memory; no multicast of any kind.
 #include <cstring>
 
@@ -31,12 +32,25 @@
 namespace b2a {
 namespace exch {
 
-constexpr int kThreads = 128;  // >= D (64 or 128) and >= W
+constexpr int kThreads = 160;  // > D (64 or 128): the last thread carries l
 constexpr int kMaxWorld = 64;
 constexpr uint64_t kExchangeLimitNs = 1000000000ull;  // 1 s
 
-__host__ __device__ inline size_t data_floats(int BH, int W, int D) {
+// 8-byte {value, call} words of the data region
+__host__ __device__ inline size_t data_words(int BH, int W, int D) {
   return (size_t)2 * W * BH * (D + 1);
+}
+
+__device__ __forceinline__ void st_tagged(uint2* dst, float v, uint32_t call) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(dst), "r"(__float_as_uint(v)),
+               "r"(call)
+               : "memory");
+}
+__device__ __forceinline__ uint2 ld_tagged(const uint2* src) {
+  uint2 r;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(src)
+               : "memory");
+  return r;
 }
 
 template <int OUT>
@@ -45,13 +59,13 @@ __global__ void __launch_bounds__(kThreads)
                             const uint64_t* __restrict__ peers, int rank, int W, int BH, int S,
                             int D, void* __restrict__ out, float* __restrict__ lse) {
   __shared__ float red[kThreads / 32];
-  __shared__ float s_w[kMaxWorld];
-  __shared__ uint32_t s_target;
+  __shared__ float s_l[kMaxWorld];
+  __shared__ uint32_t s_call;
+  __shared__ int s_timeout;
   const int bh = blockIdx.x;
   const int tid = threadIdx.x;
-  float* local = reinterpret_cast<float*>(peers[rank]);
-  uint32_t* flags = reinterpret_cast<uint32_t*>(local + data_floats(BH, W, D));
-  uint32_t* seen = flags + (size_t)W * BH;
+  uint2* local = reinterpret_cast<uint2*>(peers[rank]);
+  uint32_t* seen = reinterpret_cast<uint32_t*>(local + data_words(BH, W, D));
 
   auto block_reduce = [&](float v, bool is_max) {
 #pragma unroll
@@ -68,6 +82,10 @@ __global__ void __launch_bounds__(kThreads)
     return r;
   };
 
+  if (tid == 0) {
+    s_call = *reinterpret_cast<volatile uint32_t*>(seen + bh) + 1u;
+    s_timeout = 0;
+  }
   // 1. merge this rank's S splits
   const float* lp = l_part + (size_t)bh * S;
   const float* op = o_part + (size_t)bh * S * D;
@@ -88,58 +106,51 @@ __global__ void __launch_bounds__(kThreads)
     if (s < S) a0 += ((lp[s] == -INFINITY) ? 0.f : expf(lp[s] - M)) * op[(size_t)s * D + tid];
     acc = a0 + a1;
   }
-  const float sum = block_reduce(psum, false);
+  const float sum = block_reduce(psum, false);  // its barriers also publish s_call
   const float o_m = sum > 0.f ? acc / sum : 0.f;
   const float l_m = sum > 0.f ? M + logf(sum) : -INFINITY;
 
-  // 2. deliver (o_m, l_m) to every rank, then signal
-  if (tid == 0) s_target = *reinterpret_cast<volatile uint32_t*>(seen + bh) + 1u;
-  __syncthreads();
-  const uint32_t target = s_target;
-  const int par = (int)(target & 1u);
+  // 2. deliver the tagged (o_m, l_m) words to every rank
+  const uint32_t call = s_call;
+  const int par = (int)(call & 1u);
   const size_t slot = (((size_t)par * W + rank) * BH + bh) * (D + 1);
   for (int p = 0; p < W; ++p) {
-    float* dst = reinterpret_cast<float*>(peers[p]) + slot;
-    if (tid < D) dst[tid] = o_m;
-    if (tid == 0) dst[D] = l_m;
-  }
-  __threadfence_system();  // this thread's stores are visible before the signal
-  __syncthreads();
-  if (tid < W) {
-    uint32_t* f = reinterpret_cast<uint32_t*>(reinterpret_cast<float*>(peers[tid]) +
-                                              data_floats(BH, W, D)) +
-                  (size_t)rank * BH + bh;
-    *reinterpret_cast<volatile uint32_t*>(f) = target;
+    uint2* dst = reinterpret_cast<uint2*>(peers[p]) + slot;
+    if (tid < D) st_tagged(dst + tid, o_m, call);
+    if (tid == 0) st_tagged(dst + D, l_m, call);
   }
 
-  // 3. wait for every rank's delivery of this call, bounded
-  if (tid < W) {
-    volatile uint32_t* f = flags + (size_t)tid * BH + bh;
-    if ((int)(*f - target) < 0) {
-      const uint64_t t0 = globaltimer();
-      while ((int)(*f - target) < 0) {
+  // 3. poll this rank's own slots of the row until every word carries `call`
+  const uint2* base = local + (((size_t)par * W) * BH + bh) * (D + 1);
+  const size_t rstride = (size_t)BH * (D + 1);
+  const uint64_t t0 = globaltimer();
+  float o_r[kMaxWorld];  // this thread's column of every rank's partial
+  for (int r = 0; r < W; ++r) {
+    if (tid < D || tid == kThreads - 1) {
+      const uint2* src = base + r * rstride + (tid < D ? tid : D);
+      uint2 w = ld_tagged(src);
+      while (w.y != call && !*reinterpret_cast<volatile int*>(&s_timeout)) {
         if (globaltimer() - t0 > kExchangeLimitNs) {
           atomicOr(&g_error_flags, kErrWaitTimeout);
+          s_timeout = 1;
           break;
         }
+        w = ld_tagged(src);
       }
+      if (tid < D) o_r[r] = __uint_as_float(w.x);
+      else s_l[r] = __uint_as_float(w.x);
     }
   }
-  __threadfence_system();
   __syncthreads();
 
-  // combine the W delivered partials (local memory, written by the peers)
-  const float* base = local + (((size_t)par * W) * BH + bh) * (D + 1);
-  const size_t rstride = (size_t)BH * (D + 1);
-  if (tid < W) s_w[tid] = __ldcg(base + tid * rstride + D);
-  __syncthreads();
+  // combine the W delivered partials
   float M2 = -INFINITY;
-  for (int r = 0; r < W; ++r) M2 = fmaxf(M2, s_w[r]);
+  for (int r = 0; r < W; ++r) M2 = fmaxf(M2, s_l[r]);
   float sum2 = 0.f, acc2 = 0.f;
   for (int r = 0; r < W; ++r) {
-    const float w = (s_w[r] == -INFINITY) ? 0.f : expf(s_w[r] - M2);
+    const float w = (s_l[r] == -INFINITY) ? 0.f : expf(s_l[r] - M2);
     sum2 += w;
-    if (tid < D) acc2 += w * __ldcg(base + r * rstride + tid);
+    if (tid < D) acc2 += w * o_r[r];
   }
   if (tid < D) {
     const float o = sum2 > 0.f ? acc2 / sum2 : 0.f;
@@ -149,7 +160,7 @@ __global__ void __launch_bounds__(kThreads)
   if (lse != nullptr && tid == 0) lse[bh] = sum2 > 0.f ? M2 + logf(sum2) : -INFINITY;
   // 4. this call is complete here (a timed-out call still advances, so the
   // ranks stay in step; its output is undefined and error bit 0 is set)
-  if (tid == 0) seen[bh] = target;
+  if (tid == 0) seen[bh] = call;
 }
 
 }  // namespace exch
@@ -165,7 +176,7 @@ extern "C" {
 int64_t b2a_exchange_bytes(int B, int H, int D, int world) {
   if (B <= 0 || H <= 0 || D <= 0 || world <= 0) return -1;
   const size_t BH = (size_t)B * H;
-  const size_t bytes = exch::data_floats((int)BH, world, D) * 4 + ((size_t)world + 1) * BH * 4;
+  const size_t bytes = exch::data_words((int)BH, world, D) * 8 + BH * 4;
   return (int64_t)((bytes + 255) / 256 * 256);
 }
 

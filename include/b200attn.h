@@ -171,8 +171,10 @@ int b2a_decode_combine_ranks(const float* o_part, const float* l_part, void* o,
  * peers[r] = rank r's buffer as mapped here (peers[rank] = the own buffer).
  * A call merges this rank's split partials o_part [B,H,splits,D] / l_part
  * [B,H,splits] (from b2a_decode_splitkv on its contiguous KV slice), stores
- * the merged partial into every rank's buffer, waits (bounded, 1 s; bit 0 of
- * the device error word on timeout) for every rank's, and writes O [B,H,D]
+ * the merged partial into every rank's buffer as 8-byte words tagged with
+ * the call count, polls its own buffer (bounded, 1 s; bit 0 of the device
+ * error word on timeout) until every rank's words of this call are there,
+ * and writes O [B,H,D]
  * (dtype) and lse [B,H] (may be NULL) -- identical on every rank.  Every rank
  * must make the same sequence of calls with the same B, H, D; calls on one
  * rank must be ordered (one stream); nothing is reset between calls.  It
