@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // own sum, lse = log sum exp over all splits -- the form of one split).
 // kCombineThreads threads: the (rank, split) entries are spread over the
 // threads for the max and the weights (one load each, all in flight at once),
-// and every output column then sums its entries with several loads in flight,
+// and every output column then sums its entries with eight loads in flight,
 // so the latency of one partial's load is paid a few times, not once per split.
 constexpr int kCombineThreads = 128;
 constexpr int kCombineChunk = 1024;  // weights held in shared memory at a time
@@ -418,16 +418,15 @@ __global__ void __launch_bounds__(kCombineThreads)
     }
     __syncthreads();
     if (d < D) {
-      int i = 0;
-      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-      for (; i + 4 <= cn; i += 4) {
-        a0 += sw[i] * op(c0 + i)[d];
-        a1 += sw[i + 1] * op(c0 + i + 1)[d];
-        a2 += sw[i + 2] * op(c0 + i + 2)[d];
-        a3 += sw[i + 3] * op(c0 + i + 3)[d];
+      // eight entries' loads in flight at a time
+      for (int i0 = 0; i0 < cn; i0 += 8) {
+        float ov[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ov[i] = op(c0 + min(i0 + i, cn - 1))[d];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (i0 + i < cn) acc += sw[i0 + i] * ov[i];
       }
-      for (; i < cn; ++i) a0 += sw[i] * op(c0 + i)[d];
-      acc += (a0 + a1) + (a2 + a3);
     }
   }
   const float sum = block_reduce(psum, red, false);

@@ -95,16 +95,19 @@ __global__ void __launch_bounds__(kThreads)
   float psum = 0.f, acc = 0.f;
   for (int s = tid; s < S; s += kThreads) psum += (lp[s] == -INFINITY) ? 0.f : expf(lp[s] - M);
   if (tid < D) {
-    float a0 = 0.f, a1 = 0.f;
-    int s = 0;
-    for (; s + 2 <= S; s += 2) {
-      const float w0 = (lp[s] == -INFINITY) ? 0.f : expf(lp[s] - M);
-      const float w1 = (lp[s + 1] == -INFINITY) ? 0.f : expf(lp[s + 1] - M);
-      a0 += w0 * op[(size_t)s * D + tid];
-      a1 += w1 * op[(size_t)(s + 1) * D + tid];
+    // eight splits' loads in flight at a time (the partials sit in L2)
+    for (int s0 = 0; s0 < S; s0 += 8) {
+      float ov[8], lv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int s = min(s0 + i, S - 1);
+        ov[i] = op[(size_t)s * D + tid];
+        lv[i] = lp[s];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (s0 + i < S && lv[i] != -INFINITY) acc += expf(lv[i] - M) * ov[i];
     }
-    if (s < S) a0 += ((lp[s] == -INFINITY) ? 0.f : expf(lp[s] - M)) * op[(size_t)s * D + tid];
-    acc = a0 + a1;
   }
   const float sum = block_reduce(psum, false);  // its barriers also publish s_call
   const float o_m = sum > 0.f ? acc / sum : 0.f;
@@ -125,20 +128,41 @@ __global__ void __launch_bounds__(kThreads)
   const size_t rstride = (size_t)BH * (D + 1);
   const uint64_t t0 = globaltimer();
   float o_r[kMaxWorld];  // this thread's column of every rank's partial
-  for (int r = 0; r < W; ++r) {
-    if (tid < D || tid == kThreads - 1) {
-      const uint2* src = base + r * rstride + (tid < D ? tid : D);
-      uint2 w = ld_tagged(src);
-      while (w.y != call && !*reinterpret_cast<volatile int*>(&s_timeout)) {
-        if (globaltimer() - t0 > kExchangeLimitNs) {
-          atomicOr(&g_error_flags, kErrWaitTimeout);
-          s_timeout = 1;
-          break;
+  if (tid < D || tid == kThreads - 1) {
+    const int col = tid < D ? tid : D;
+    // eight ranks' words in flight per poll round
+    for (int r0 = 0; r0 < W; r0 += 8) {
+      const int nr = min(8, W - r0);
+      uint32_t pending = (1u << nr) - 1u;
+      while (pending != 0u) {
+        uint2 w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if ((pending >> i) & 1u) w[i] = ld_tagged(base + (size_t)(r0 + i) * rstride + col);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (((pending >> i) & 1u) && w[i].y == call) {
+            if (tid < D) o_r[r0 + i] = __uint_as_float(w[i].x);
+            else s_l[r0 + i] = __uint_as_float(w[i].x);
+            pending &= ~(1u << i);
+          }
         }
-        w = ld_tagged(src);
+        if (pending != 0u) {
+          if (*reinterpret_cast<volatile int*>(&s_timeout)) break;
+          if (globaltimer() - t0 > kExchangeLimitNs) {
+            atomicOr(&g_error_flags, kErrWaitTimeout);
+            s_timeout = 1;
+            break;
+          }
+        }
       }
-      if (tid < D) o_r[r] = __uint_as_float(w.x);
-      else s_l[r] = __uint_as_float(w.x);
+      if (pending != 0u) {  // timed out: this rank's words are missing; count them as empty
+        for (int i = 0; i < nr; ++i)
+          if ((pending >> i) & 1u) {
+            if (tid < D) o_r[r0 + i] = 0.f;
+            else s_l[r0 + i] = -INFINITY;
+          }
+      }
     }
   }
   __syncthreads();
